@@ -1,0 +1,223 @@
+#ifndef SPECDECODE_CUDA_H
+#define SPECDECODE_CUDA_H
+
+/*
+ * C ABI of libspecdecode_cuda.so: the paged INT8 KV-cache hot path on B200
+ * (sm_100a).  The library is the device-side replacement for the reference
+ * project's CPU quantizer library (native/include/specdecode/native.h) and for
+ * the PyTorch ops its packed CUDA storage and unfused attention use
+ * (src/specdecode/cuda_kv_cache.py).
+ *
+ * Conventions, kept from native/include/specdecode/native.h and
+ * docs/native.md:41-56 of the reference:
+ *   - every function returns an sdc_status_t; outputs go through caller-owned
+ *     pointers; nothing returned is ever allocated by the library;
+ *   - arguments are validated on the host before any launch or output write;
+ *   - C++ exceptions never cross the boundary;
+ *   - no fast-math anywhere.
+ * Additions for device work:
+ *   - device buffers are plain pointers into the current CUDA device's
+ *     memory; `stream` is a cudaStream_t passed as uintptr_t (0 = legacy
+ *     default stream); launches are asynchronous on that stream;
+ *   - faults that only the kernel can see (a slot or block id outside the
+ *     pool, a non-finite input, an invalid scale, a wait that gave up) are
+ *     OR-ed into a caller-provided device status word (int32, SDC_FAULT_*
+ *     bits) instead of trapping; the host reads it when it next synchronizes;
+ *   - calls are thread-safe when callers use distinct streams, status words
+ *     and workspaces.
+ */
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__) || defined(__clang__)
+#define SDC_API __attribute__((visibility("default")))
+#else
+#define SDC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SDC_ABI_VERSION UINT32_C(0x00020001)
+
+/* Values 0-10 keep the meaning they have in the reference's sd_status_t
+ * (native/include/specdecode/native.h:25-37). */
+typedef enum sdc_status {
+    SDC_STATUS_OK = 0,
+    SDC_STATUS_NULL_ARGUMENT = 1,
+    SDC_STATUS_INVALID_SIZE = 2,
+    SDC_STATUS_NONFINITE_VALUE = 3,
+    SDC_STATUS_OVERFLOW = 8,
+    SDC_STATUS_INTERNAL_ERROR = 9,
+    SDC_STATUS_INVALID_SCALE = 10,
+    SDC_STATUS_CUDA_ERROR = 11,
+    SDC_STATUS_UNSUPPORTED = 12,
+    SDC_STATUS_MISALIGNED = 13,
+    SDC_STATUS_DEVICE_FAULT = 14,
+    SDC_STATUS_INVALID_ARGUMENT = 15
+} sdc_status_t;
+
+/* Bits a kernel ORs into the device status word. */
+#define SDC_FAULT_NONFINITE_VALUE  0x01
+#define SDC_FAULT_INVALID_SCALE    0x02
+#define SDC_FAULT_SLOT_RANGE       0x04
+#define SDC_FAULT_BLOCK_RANGE      0x08
+#define SDC_FAULT_CONTEXT_RANGE    0x10
+#define SDC_FAULT_WAIT_TIMEOUT     0x20
+#define SDC_FAULT_TABLE_RANGE      0x40
+
+typedef enum sdc_dtype {
+    SDC_DTYPE_F32 = 0,
+    SDC_DTYPE_BF16 = 1,
+    SDC_DTYPE_F16 = 2,
+    SDC_DTYPE_F64 = 3
+} sdc_dtype_t;
+
+/*
+ * The paged pool.  Codes are int8, scales float32, one scale per
+ * (block, offset, layer, head) for keys and one for values.  Within a page a
+ * (block, layer, head) holds block_size token rows of head_dim codes
+ * back to back (token stride = head_dim) and block_size scales back to back
+ * (token stride = 1); the other strides are free, in elements.  The library's
+ * own allocation uses [block][layer][head][offset][dim]; the reference's
+ * logical view [block][offset][layer][head][dim] is a permutation of it.
+ */
+typedef struct sdc_page_pool {
+    int8_t* keys;
+    int8_t* values;
+    float* key_scales;
+    float* value_scales;
+    int64_t num_blocks;
+    int64_t block_size;
+    int64_t num_layers;
+    int64_t num_heads;
+    int64_t head_dim;
+    int64_t code_block_stride;
+    int64_t code_layer_stride;
+    int64_t code_head_stride;
+    int64_t scale_block_stride;
+    int64_t scale_layer_stride;
+    int64_t scale_head_stride;
+} sdc_page_pool_t;
+
+/*
+ * Device block tables and lengths, plus a list of edits to apply.
+ * entries: [num_entries][3] int32 (row, logical block, physical block; -1 clears)
+ * lengths: [num_lengths][2] int32 (row, new context length)
+ */
+typedef struct sdc_table_edits {
+    int32_t* block_tables;
+    int64_t table_stride;
+    int64_t table_rows;
+    int32_t* context_lens;
+    const int32_t* entries;
+    int64_t num_entries;
+    const int32_t* lengths;
+    int64_t num_lengths;
+} sdc_table_edits_t;
+
+SDC_API uint32_t sdc_abi_version(void);
+SDC_API const char* sdc_status_string(sdc_status_t status);
+
+/*
+ * Host-buffer drop-ins for the reference's per-vector quantizer, with the
+ * reference's exact signatures and semantics:
+ *   replaces sd_quantize_symmetric_int8_f64   (native/include/specdecode/native.h:93-98,
+ *                                              native/src/native.cpp:275-319)
+ *   replaces sd_dequantize_symmetric_int8_f64 (native/include/specdecode/native.h:101-106,
+ *                                              native/src/native.cpp:321-353)
+ * The arithmetic runs on the current CUDA device; inputs are copied in and
+ * results copied back before return, and outputs are written only on success.
+ */
+SDC_API sdc_status_t sdc_quantize_symmetric_int8_f64(
+    const double* values, size_t count, int8_t* output_values, double* output_scale);
+SDC_API sdc_status_t sdc_dequantize_symmetric_int8_f64(
+    const int8_t* values, size_t count, double scale, double* output_values);
+
+/*
+ * Quantize `rows` device vectors of `count` elements (row-major, dtype
+ * `src_dtype`) with the reference rule; per-row status codes (sd_status_t
+ * numbering) go to `row_status`.  Rows with a non-zero status are not written.
+ * Batched form of the same per-vector rule (src/specdecode/kv_cache.py:130-146).
+ */
+SDC_API sdc_status_t sdc_quantize_rows(
+    const void* source, int src_dtype, int64_t rows, int64_t count,
+    int8_t* codes, float* scales, int32_t* row_status, uintptr_t stream);
+
+/*
+ * Kernel (a): fused quantize-and-append.  For every token i, every layer in
+ * [layer_begin, layer_begin + num_src_layers) and every head, quantizes
+ * keys[i][layer - layer_begin][head][:] and values[...] (dtype src_dtype,
+ * element strides src_token_stride / src_layer_stride / src_head_stride, dim
+ * contiguous) and writes codes + scale into physical slot slot_mapping[i]
+ * (block = slot / block_size, offset = slot % block_size) with 16-byte stores.
+ * Optional `edits` (may be NULL) are applied in the same launch.
+ * Replaces: PagedKVCache.append_many's quantize+write (src/specdecode/kv_cache.py:298-336)
+ * and CudaPagedKVCacheStorage's scatter upload (src/specdecode/cuda_kv_cache.py:343-348).
+ * Requires head_dim % 16 == 0 and head_dim <= 512.
+ */
+SDC_API sdc_status_t sdc_quantize_append(
+    const sdc_page_pool_t* pool, int64_t layer_begin, int64_t num_src_layers,
+    const void* keys, const void* values, int src_dtype,
+    int64_t num_tokens, int64_t src_token_stride, int64_t src_layer_stride,
+    int64_t src_head_stride, const int64_t* slot_mapping, const sdc_table_edits_t* edits,
+    int32_t* device_status, uintptr_t stream);
+
+/*
+ * Kernel (b): rollback.  Zeroes codes and scales of every layer and head in
+ * the `num_clear` physical slots of `clear_slots`, then applies `edits`
+ * (rewound block-table entries set to -1, new context lengths).
+ * Replaces: PagedKVCache.truncate / rollback (src/specdecode/kv_cache.py:382-420)
+ * and the stale-slot clearing of src/specdecode/cuda_kv_cache.py:336-342.
+ */
+SDC_API sdc_status_t sdc_rollback(
+    const sdc_page_pool_t* pool, const int64_t* clear_slots, int64_t num_clear,
+    const sdc_table_edits_t* edits, int32_t* device_status, uintptr_t stream);
+
+/* Workspace bytes sdc_paged_verify_attention needs for this shape. */
+SDC_API sdc_status_t sdc_paged_attention_workspace_size(
+    int64_t batch, int64_t num_query_heads, int64_t num_kv_heads, int64_t head_dim,
+    int64_t window, int64_t max_context_len, size_t* bytes);
+
+/*
+ * Kernel (c): fused paged verify/decode attention (split-K flash decoding).
+ * query/out: [batch][num_query_heads][window][head_dim], dtype query_dtype
+ * (bf16, f16 or f32), contiguous.  The window holds the last `window` cached
+ * positions of each sequence; query head h reads KV head h / (Hq / Hkv); a
+ * query at position p sees keys at positions <= p; softmax scale 1/sqrt(D).
+ * block_tables: device int32 [batch][table_stride]; context_lens: device int32
+ * [batch]; max_context_len: a host-side upper bound on every context length.
+ * Replaces: submit_paged_attention's gather/dequantize/GQA/mask/SDPA
+ * (src/specdecode/cuda_kv_cache.py:370-503, computation at :452-497) and the
+ * CPU reconstruct path feeding attention (src/specdecode/hf_paged_cache.py:247-313).
+ */
+SDC_API sdc_status_t sdc_paged_verify_attention(
+    const sdc_page_pool_t* pool, int64_t layer, const void* query, int query_dtype,
+    int64_t batch, int64_t num_query_heads, int64_t window, const int32_t* block_tables,
+    int64_t table_stride, const int32_t* context_lens, int64_t max_context_len, void* out,
+    void* workspace, size_t workspace_bytes, int32_t* device_status, uintptr_t stream);
+
+/*
+ * Gather and dequantize cached tokens: for every slot i and layer in
+ * [layer_begin, layer_begin + num_layers) and head, writes code * scale to
+ * out_keys / out_values at i*out_token_stride + (layer-layer_begin)*out_layer_stride
+ * + head*out_head_stride (dim contiguous) in out_dtype.  f64 output is exact;
+ * f32 is the correctly rounded product; bf16/f16 narrow through float32, as
+ * torch.tensor does for Python floats.
+ * Replaces: PagedKVCache.read_token / read_sequence dequantization
+ * (src/specdecode/kv_cache.py:349-380) and the CPU reconstruct of
+ * HuggingFacePagedCacheMirror.materialize_legacy_cache (src/specdecode/hf_paged_cache.py:247-313).
+ */
+SDC_API sdc_status_t sdc_gather_dequantize(
+    const sdc_page_pool_t* pool, int64_t layer_begin, int64_t num_layers,
+    const int64_t* slot_mapping, int64_t num_tokens, void* out_keys, void* out_values,
+    int out_dtype, int64_t out_token_stride, int64_t out_layer_stride, int64_t out_head_stride,
+    int32_t* device_status, uintptr_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

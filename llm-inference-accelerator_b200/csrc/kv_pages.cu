@@ -1,0 +1,677 @@
+// Kernels (a) quantize-and-append and (b) rollback, plus the per-vector
+// quantizer and the gather/dequantize read path, with their C ABI entries.
+//
+// Work mapping shared by the page kernels: a "head vector" is the head_dim
+// codes of one (token, layer, K|V, head).  A group of LPV lanes owns one head
+// vector; lane j of the group owns elements [16j, 16j + 16), so every code
+// store is one 16-byte store and a group writes the vector's row in one
+// coalesced burst.  Vectors are enumerated with the head fastest, so
+// neighbouring groups read neighbouring source rows.
+
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <type_traits>
+#include <vector>
+
+#include "host_common.h"
+
+namespace sdc {
+namespace {
+
+template <typename Src>
+struct AccOf {
+    using type = float;
+};
+template <>
+struct AccOf<double> {
+    using type = double;
+};
+
+__device__ __forceinline__ float amax(float a, float b) { return fmaxf(a, b); }
+__device__ __forceinline__ double amax(double a, double b) { return fmax(a, b); }
+
+template <typename Src>
+__device__ __forceinline__ int quant_one(typename AccOf<Src>::type x, float s) {
+    if constexpr (std::is_same<Src, double>::value) {
+        return quant_code_f64(x, static_cast<double>(s));
+    } else {
+        return s >= kFloatPathMinScale ? quant_code_f32(x, s)
+                                       : quant_code_f64(static_cast<double>(x), static_cast<double>(s));
+    }
+}
+
+struct AppendArgs {
+    Pool pool;
+    const void* keys;
+    const void* values;
+    int64_t layer_begin;
+    int64_t num_src_layers;
+    int64_t s_tok, s_layer, s_head;
+    const int64_t* slots;
+    int64_t total_vectors;
+    int64_t vector_blocks;
+    TableEdits edits;
+    int32_t* status;
+};
+
+template <typename Src, int LPV>
+__global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
+    using Acc = typename AccOf<Src>::type;
+    if (blockIdx.x >= a.vector_blocks) {  // the trailing block applies table edits
+        apply_table_edits(a.edits, threadIdx.x, blockDim.x, a.status);
+        return;
+    }
+    constexpr int VPW = 32 / LPV;
+    const int lane = threadIdx.x & 31;
+    const int sub = lane & (LPV - 1);
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t v = warp * VPW + lane / LPV;
+    const bool active = v < a.total_vectors;
+    const int64_t H = a.pool.num_heads;
+    const int64_t D = a.pool.head_dim;
+
+    int64_t head = 0, kv = 0, layer_rel = 0, token = 0;
+    if (active) {
+        head = v % H;
+        int64_t r = v / H;
+        kv = r & 1;
+        r >>= 1;
+        layer_rel = r % a.num_src_layers;
+        token = r / a.num_src_layers;
+    }
+    const bool has_chunk = active && (sub * 16 < D);
+
+    Acc x[16];
+    if (has_chunk) {
+        const Src* base = static_cast<const Src*>(kv ? a.values : a.keys) + token * a.s_tok +
+                          layer_rel * a.s_layer + head * a.s_head + sub * 16;
+        load16(base, x);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) x[i] = Acc(0);
+    }
+    int bad = 0;
+    Acc m = Acc(0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        bad |= !isfinite(x[i]);
+        m = amax(m, fabs(x[i]));
+    }
+#pragma unroll
+    for (int off = LPV / 2; off > 0; off >>= 1) {
+        m = amax(m, __shfl_xor_sync(kFullMask, m, off));
+        bad |= __shfl_xor_sync(kFullMask, bad, off);
+    }
+    if (!active) return;
+
+    const int64_t slot = __ldg(a.slots + token);
+    if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
+        if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
+        return;
+    }
+    if (bad) {
+        if (sub == 0) report_fault(a.status, SDC_FAULT_NONFINITE_VALUE);
+        return;
+    }
+    const int64_t blk = slot / a.pool.block_size;
+    const int64_t off = slot - blk * a.pool.block_size;
+    const int64_t layer = a.layer_begin + layer_rel;
+    int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
+                    head * a.pool.chs + off * D;
+    float* scale_dst = (kv ? a.pool.value_scales : a.pool.key_scales) + blk * a.pool.sbs +
+                       layer * a.pool.sls + head * a.pool.shs + off;
+
+    float s = 0.0f;
+    uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+    if (m != Acc(0)) {
+        s = scale_from_max(static_cast<double>(m));
+        if (!(s > 0.0f) || isinf(s)) {
+            if (sub == 0) report_fault(a.status, SDC_FAULT_INVALID_SCALE);
+            return;
+        }
+        int q[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q[i] = quant_one<Src>(x[i], s);
+        packed.x = pack4(q[0], q[1], q[2], q[3]);
+        packed.y = pack4(q[4], q[5], q[6], q[7]);
+        packed.z = pack4(q[8], q[9], q[10], q[11]);
+        packed.w = pack4(q[12], q[13], q[14], q[15]);
+    }
+    if (has_chunk) *reinterpret_cast<uint4*>(codes + sub * 16) = packed;
+    if (sub == 0) *scale_dst = s;
+}
+
+// One warp per row, any row length: the per-vector API and the
+// KVQuantizer-protocol path use it.
+template <typename Src>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const Src* src, int64_t rows, int64_t count,
+                                                            int8_t* codes, float* scales,
+                                                            int32_t* row_status) {
+    using Acc = typename AccOf<Src>::type;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (row >= rows) return;
+    const Src* x = src + row * count;
+    Acc m = Acc(0);
+    int bad = 0;
+    for (int64_t i = lane; i < count; i += 32) {
+        const Acc v = static_cast<Acc>(x[i]);
+        bad |= !isfinite(v);
+        m = amax(m, fabs(v));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        m = amax(m, __shfl_xor_sync(kFullMask, m, off));
+        bad |= __shfl_xor_sync(kFullMask, bad, off);
+    }
+    if (bad) {
+        if (lane == 0) row_status[row] = SDC_STATUS_NONFINITE_VALUE;
+        return;
+    }
+    int8_t* out = codes + row * count;
+    if (m == Acc(0)) {
+        for (int64_t i = lane; i < count; i += 32) out[i] = 0;
+        if (lane == 0) {
+            scales[row] = 0.0f;
+            row_status[row] = SDC_STATUS_OK;
+        }
+        return;
+    }
+    const float s = scale_from_max(static_cast<double>(m));
+    if (!(s > 0.0f) || isinf(s)) {
+        if (lane == 0) row_status[row] = SDC_STATUS_INVALID_SCALE;
+        return;
+    }
+    for (int64_t i = lane; i < count; i += 32) {
+        out[i] = static_cast<int8_t>(quant_one<Src>(static_cast<Acc>(x[i]), s));
+    }
+    if (lane == 0) {
+        scales[row] = s;
+        row_status[row] = SDC_STATUS_OK;
+    }
+}
+
+__global__ void dequantize_vector_kernel(const int8_t* codes, int64_t count, double scale, double* out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < count) out[i] = static_cast<double>(codes[i]) * scale;
+}
+
+struct RollbackArgs {
+    Pool pool;
+    const int64_t* slots;
+    int64_t total_vectors;
+    int64_t vector_blocks;
+    TableEdits edits;
+    int32_t* status;
+};
+
+template <int LPV>
+__global__ void __launch_bounds__(256) rollback_kernel(RollbackArgs a) {
+    if (blockIdx.x >= a.vector_blocks) {
+        apply_table_edits(a.edits, threadIdx.x, blockDim.x, a.status);
+        return;
+    }
+    constexpr int VPW = 32 / LPV;
+    const int lane = threadIdx.x & 31;
+    const int sub = lane & (LPV - 1);
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t v = warp * VPW + lane / LPV;
+    if (v >= a.total_vectors) return;
+    const int64_t H = a.pool.num_heads;
+    const int64_t D = a.pool.head_dim;
+    const int64_t head = v % H;
+    int64_t r = v / H;
+    const int64_t kv = r & 1;
+    r >>= 1;
+    const int64_t layer = r % a.pool.num_layers;
+    const int64_t index = r / a.pool.num_layers;
+    const int64_t slot = __ldg(a.slots + index);
+    if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
+        if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
+        return;
+    }
+    const int64_t blk = slot / a.pool.block_size;
+    const int64_t off = slot - blk * a.pool.block_size;
+    if (sub * 16 < D) {
+        int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
+                        head * a.pool.chs + off * D + sub * 16;
+        *reinterpret_cast<uint4*>(codes) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (sub == 0) {
+        float* sc = (kv ? a.pool.value_scales : a.pool.key_scales) + blk * a.pool.sbs +
+                    layer * a.pool.sls + head * a.pool.shs + off;
+        *sc = 0.0f;
+    }
+}
+
+struct GatherArgs {
+    Pool pool;
+    int64_t layer_begin;
+    int64_t num_layers;
+    const int64_t* slots;
+    int64_t total_vectors;
+    void* out_keys;
+    void* out_values;
+    int64_t o_tok, o_layer, o_head;
+    int32_t* status;
+};
+
+__device__ __forceinline__ void store16(double* p, const int (&q)[16], float s) {
+    double2* d = reinterpret_cast<double2*>(p);
+    const double sd = static_cast<double>(s);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = make_double2(q[2 * i] * sd, q[2 * i + 1] * sd);
+}
+__device__ __forceinline__ void store16(float* p, const int (&q)[16], float s) {
+    float4* d = reinterpret_cast<float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        d[i] = make_float4(__fmul_rn(static_cast<float>(q[4 * i]), s), __fmul_rn(static_cast<float>(q[4 * i + 1]), s),
+                           __fmul_rn(static_cast<float>(q[4 * i + 2]), s), __fmul_rn(static_cast<float>(q[4 * i + 3]), s));
+    }
+}
+__device__ __forceinline__ void store16(__nv_bfloat16* p, const int (&q)[16], float s) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(__fmul_rn(static_cast<float>(q[2 * i]), s),
+                                                 __fmul_rn(static_cast<float>(q[2 * i + 1]), s));
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    uint4* d = reinterpret_cast<uint4*>(p);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+__device__ __forceinline__ void store16(__half* p, const int (&q)[16], float s) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        __half2 h = __floats2half2_rn(__fmul_rn(static_cast<float>(q[2 * i]), s),
+                                      __fmul_rn(static_cast<float>(q[2 * i + 1]), s));
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    uint4* d = reinterpret_cast<uint4*>(p);
+    d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+template <typename Out, int LPV>
+__global__ void __launch_bounds__(256) gather_dequantize_kernel(GatherArgs a) {
+    constexpr int VPW = 32 / LPV;
+    const int lane = threadIdx.x & 31;
+    const int sub = lane & (LPV - 1);
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t v = warp * VPW + lane / LPV;
+    if (v >= a.total_vectors) return;
+    const int64_t H = a.pool.num_heads;
+    const int64_t D = a.pool.head_dim;
+    const int64_t head = v % H;
+    int64_t r = v / H;
+    const int64_t kv = r & 1;
+    r >>= 1;
+    const int64_t layer_rel = r % a.num_layers;
+    const int64_t token = r / a.num_layers;
+    const int64_t slot = __ldg(a.slots + token);
+    if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
+        if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
+        return;
+    }
+    if (sub * 16 >= D) return;
+    const int64_t blk = slot / a.pool.block_size;
+    const int64_t off = slot - blk * a.pool.block_size;
+    const int64_t layer = a.layer_begin + layer_rel;
+    const int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
+                          head * a.pool.chs + off * D + sub * 16;
+    const float s = __ldg((kv ? a.pool.value_scales : a.pool.key_scales) + blk * a.pool.sbs +
+                          layer * a.pool.sls + head * a.pool.shs + off);
+    const uint4 packed = __ldg(reinterpret_cast<const uint4*>(codes));
+    const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
+    int q[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = static_cast<int8_t>((w[i / 4] >> (8 * (i % 4))) & 0xffu);
+    Out* dst = static_cast<Out*>(kv ? a.out_values : a.out_keys) + token * a.o_tok + layer_rel * a.o_layer +
+               head * a.o_head + sub * 16;
+    store16(dst, q, s);
+}
+
+constexpr int kThreads = 256;
+
+template <typename Src>
+sdc_status_t launch_append(int lpv, int64_t blocks, cudaStream_t stream, const AppendArgs& a) {
+    switch (lpv) {
+        case 1: quantize_append_kernel<Src, 1><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 2: quantize_append_kernel<Src, 2><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 4: quantize_append_kernel<Src, 4><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 8: quantize_append_kernel<Src, 8><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 16: quantize_append_kernel<Src, 16><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 32: quantize_append_kernel<Src, 32><<<blocks, kThreads, 0, stream>>>(a); break;
+        default: return SDC_STATUS_UNSUPPORTED;
+    }
+    return launch_status();
+}
+
+template <typename Out>
+sdc_status_t launch_gather(int lpv, int64_t blocks, cudaStream_t stream, const GatherArgs& a) {
+    switch (lpv) {
+        case 1: gather_dequantize_kernel<Out, 1><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 2: gather_dequantize_kernel<Out, 2><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 4: gather_dequantize_kernel<Out, 4><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 8: gather_dequantize_kernel<Out, 8><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 16: gather_dequantize_kernel<Out, 16><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 32: gather_dequantize_kernel<Out, 32><<<blocks, kThreads, 0, stream>>>(a); break;
+        default: return SDC_STATUS_UNSUPPORTED;
+    }
+    return launch_status();
+}
+
+sdc_status_t launch_rollback(int lpv, int64_t blocks, cudaStream_t stream, const RollbackArgs& a) {
+    switch (lpv) {
+        case 1: rollback_kernel<1><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 2: rollback_kernel<2><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 4: rollback_kernel<4><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 8: rollback_kernel<8><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 16: rollback_kernel<16><<<blocks, kThreads, 0, stream>>>(a); break;
+        case 32: rollback_kernel<32><<<blocks, kThreads, 0, stream>>>(a); break;
+        default: return SDC_STATUS_UNSUPPORTED;
+    }
+    return launch_status();
+}
+
+// Blocks needed for `vectors` head vectors at `lpv` lanes per vector.
+int64_t vector_blocks(int64_t vectors, int lpv) {
+    const int64_t per_block = (kThreads / 32) * (32 / lpv);
+    return ceil_div(vectors, per_block);
+}
+
+template <typename Src>
+sdc_status_t launch_rows(const void* src, int64_t rows, int64_t count, int8_t* codes, float* scales,
+                         int32_t* status, cudaStream_t stream) {
+    const int64_t blocks = ceil_div(rows, kThreads / 32);
+    quantize_rows_kernel<Src><<<blocks, kThreads, 0, stream>>>(static_cast<const Src*>(src), rows, count, codes,
+                                                               scales, status);
+    return launch_status();
+}
+
+sdc_status_t dispatch_rows(const void* src, int dtype, int64_t rows, int64_t count, int8_t* codes, float* scales,
+                           int32_t* status, cudaStream_t stream) {
+    switch (dtype) {
+        case SDC_DTYPE_F32: return launch_rows<float>(src, rows, count, codes, scales, status, stream);
+        case SDC_DTYPE_BF16: return launch_rows<__nv_bfloat16>(src, rows, count, codes, scales, status, stream);
+        case SDC_DTYPE_F16: return launch_rows<__half>(src, rows, count, codes, scales, status, stream);
+        case SDC_DTYPE_F64: return launch_rows<double>(src, rows, count, codes, scales, status, stream);
+        default: return SDC_STATUS_UNSUPPORTED;
+    }
+}
+
+}  // namespace
+}  // namespace sdc
+
+using namespace sdc;
+
+extern "C" {
+
+SDC_API uint32_t sdc_abi_version(void) { return SDC_ABI_VERSION; }
+
+SDC_API const char* sdc_status_string(sdc_status_t status) {
+    switch (status) {
+        case SDC_STATUS_OK: return "ok";
+        case SDC_STATUS_NULL_ARGUMENT: return "null argument";
+        case SDC_STATUS_INVALID_SIZE: return "invalid size";
+        case SDC_STATUS_NONFINITE_VALUE: return "non-finite value";
+        case SDC_STATUS_OVERFLOW: return "size overflow";
+        case SDC_STATUS_INTERNAL_ERROR: return "internal error";
+        case SDC_STATUS_INVALID_SCALE: return "invalid quantization scale";
+        case SDC_STATUS_CUDA_ERROR: return "CUDA runtime error";
+        case SDC_STATUS_UNSUPPORTED: return "unsupported shape or dtype";
+        case SDC_STATUS_MISALIGNED: return "buffer or stride is not 16-byte aligned";
+        case SDC_STATUS_DEVICE_FAULT: return "a kernel reported a fault in the device status word";
+        case SDC_STATUS_INVALID_ARGUMENT: return "invalid argument";
+        default: return "unknown status";
+    }
+}
+
+SDC_API sdc_status_t sdc_quantize_symmetric_int8_f64(const double* values, size_t count, int8_t* output_values,
+                                                     double* output_scale) {
+    try {
+        if (values == nullptr || output_values == nullptr || output_scale == nullptr) {
+            return SDC_STATUS_NULL_ARGUMENT;
+        }
+        if (count == 0) return SDC_STATUS_INVALID_SIZE;
+        if (count > (size_t(1) << 40)) return SDC_STATUS_OVERFLOW;
+        cudaStream_t stream = cudaStreamPerThread;
+        const size_t in_bytes = count * sizeof(double);
+        const size_t code_off = (in_bytes + 15) & ~size_t(15);
+        const size_t scale_off = (code_off + count + 15) & ~size_t(15);
+        const size_t total = scale_off + 16;
+        char* dev = nullptr;
+        if (cudaMallocAsync(reinterpret_cast<void**>(&dev), total, stream) != cudaSuccess) {
+            return SDC_STATUS_CUDA_ERROR;
+        }
+        std::vector<int8_t> codes(count);
+        float scale = 0.0f;
+        int32_t status = SDC_STATUS_INTERNAL_ERROR;
+        sdc_status_t rc = SDC_STATUS_OK;
+        if (cudaMemcpyAsync(dev, values, in_bytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+            rc = SDC_STATUS_CUDA_ERROR;
+        }
+        if (rc == SDC_STATUS_OK) {
+            rc = launch_rows<double>(dev, 1, static_cast<int64_t>(count), reinterpret_cast<int8_t*>(dev + code_off),
+                                     reinterpret_cast<float*>(dev + scale_off),
+                                     reinterpret_cast<int32_t*>(dev + scale_off + 4), stream);
+        }
+        if (rc == SDC_STATUS_OK &&
+            (cudaMemcpyAsync(codes.data(), dev + code_off, count, cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+             cudaMemcpyAsync(&scale, dev + scale_off, 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+             cudaMemcpyAsync(&status, dev + scale_off + 4, 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess)) {
+            rc = SDC_STATUS_CUDA_ERROR;
+        }
+        cudaFreeAsync(dev, stream);
+        if (cudaStreamSynchronize(stream) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
+        if (rc != SDC_STATUS_OK) return rc;
+        if (status != SDC_STATUS_OK) return static_cast<sdc_status_t>(status);
+        std::memcpy(output_values, codes.data(), count);
+        *output_scale = static_cast<double>(scale);
+        return SDC_STATUS_OK;
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_dequantize_symmetric_int8_f64(const int8_t* values, size_t count, double scale,
+                                                       double* output_values) {
+    try {
+        if (values == nullptr || output_values == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        if (count == 0) return SDC_STATUS_INVALID_SIZE;
+        if (count > (size_t(1) << 40)) return SDC_STATUS_OVERFLOW;
+        if (!std::isfinite(scale) || scale < 0.0) return SDC_STATUS_INVALID_SCALE;
+        if (scale == 0.0) {
+            for (size_t i = 0; i < count; ++i) {
+                if (values[i] != 0) return SDC_STATUS_INVALID_SCALE;
+            }
+        }
+        cudaStream_t stream = cudaStreamPerThread;
+        const size_t out_off = (count + 15) & ~size_t(15);
+        char* dev = nullptr;
+        if (cudaMallocAsync(reinterpret_cast<void**>(&dev), out_off + count * sizeof(double), stream) !=
+            cudaSuccess) {
+            return SDC_STATUS_CUDA_ERROR;
+        }
+        std::vector<double> out(count);
+        sdc_status_t rc = SDC_STATUS_OK;
+        if (cudaMemcpyAsync(dev, values, count, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+            rc = SDC_STATUS_CUDA_ERROR;
+        }
+        if (rc == SDC_STATUS_OK) {
+            const int64_t blocks = ceil_div(static_cast<int64_t>(count), kThreads);
+            dequantize_vector_kernel<<<blocks, kThreads, 0, stream>>>(
+                reinterpret_cast<const int8_t*>(dev), static_cast<int64_t>(count), scale,
+                reinterpret_cast<double*>(dev + out_off));
+            rc = launch_status();
+        }
+        if (rc == SDC_STATUS_OK && cudaMemcpyAsync(out.data(), dev + out_off, count * sizeof(double),
+                                                   cudaMemcpyDeviceToHost, stream) != cudaSuccess) {
+            rc = SDC_STATUS_CUDA_ERROR;
+        }
+        cudaFreeAsync(dev, stream);
+        if (cudaStreamSynchronize(stream) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
+        if (rc != SDC_STATUS_OK) return rc;
+        std::memcpy(output_values, out.data(), count * sizeof(double));
+        return SDC_STATUS_OK;
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_quantize_rows(const void* source, int src_dtype, int64_t rows, int64_t count,
+                                       int8_t* codes, float* scales, int32_t* row_status, uintptr_t stream) {
+    try {
+        if (source == nullptr || codes == nullptr || scales == nullptr || row_status == nullptr) {
+            return SDC_STATUS_NULL_ARGUMENT;
+        }
+        if (rows < 0 || count < 1) return SDC_STATUS_INVALID_SIZE;
+        if (dtype_size(src_dtype) == 0) return SDC_STATUS_UNSUPPORTED;
+        if (rows == 0) return SDC_STATUS_OK;
+        return dispatch_rows(source, src_dtype, rows, count, codes, scales, row_status, as_stream(stream));
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_quantize_append(const sdc_page_pool_t* pool, int64_t layer_begin, int64_t num_src_layers,
+                                         const void* keys, const void* values, int src_dtype, int64_t num_tokens,
+                                         int64_t src_token_stride, int64_t src_layer_stride,
+                                         int64_t src_head_stride, const int64_t* slot_mapping,
+                                         const sdc_table_edits_t* edits, int32_t* device_status,
+                                         uintptr_t stream) {
+    try {
+        sdc_status_t rc = validate_pool(pool);
+        if (rc != SDC_STATUS_OK) return rc;
+        TableEdits te;
+        rc = validate_edits(edits, &te);
+        if (rc != SDC_STATUS_OK) return rc;
+        if (device_status == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        if (num_tokens < 0 || num_src_layers < 1) return SDC_STATUS_INVALID_SIZE;
+        if (layer_begin < 0 || layer_begin + num_src_layers > pool->num_layers) return SDC_STATUS_INVALID_SIZE;
+        const int es = dtype_size(src_dtype);
+        if (es == 0) return SDC_STATUS_UNSUPPORTED;
+        const bool has_edits = te.num_entries > 0 || te.num_lengths > 0;
+        if (num_tokens == 0 && !has_edits) return SDC_STATUS_OK;
+        if (num_tokens > 0) {
+            if (keys == nullptr || values == nullptr || slot_mapping == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+            if (src_token_stride < 0 || src_layer_stride < 0 || src_head_stride < 0) {
+                return SDC_STATUS_INVALID_SIZE;
+            }
+            if (!aligned16(keys) || !aligned16(values) || (src_token_stride * es) % 16 ||
+                (src_layer_stride * es) % 16 || (src_head_stride * es) % 16) {
+                return SDC_STATUS_MISALIGNED;
+            }
+        }
+        const int lpv = lanes_per_vector(pool->head_dim);
+        AppendArgs a;
+        a.pool = to_pool(pool);
+        a.keys = keys;
+        a.values = values;
+        a.layer_begin = layer_begin;
+        a.num_src_layers = num_src_layers;
+        a.s_tok = src_token_stride;
+        a.s_layer = src_layer_stride;
+        a.s_head = src_head_stride;
+        a.slots = slot_mapping;
+        a.total_vectors = num_tokens * num_src_layers * 2 * pool->num_heads;
+        a.vector_blocks = vector_blocks(a.total_vectors, lpv);
+        a.edits = te;
+        a.status = device_status;
+        const int64_t blocks = a.vector_blocks + (has_edits ? 1 : 0);
+        if (blocks > INT32_MAX) return SDC_STATUS_OVERFLOW;
+        cudaStream_t st = as_stream(stream);
+        switch (src_dtype) {
+            case SDC_DTYPE_F32: return launch_append<float>(lpv, blocks, st, a);
+            case SDC_DTYPE_BF16: return launch_append<__nv_bfloat16>(lpv, blocks, st, a);
+            case SDC_DTYPE_F16: return launch_append<__half>(lpv, blocks, st, a);
+            case SDC_DTYPE_F64: return launch_append<double>(lpv, blocks, st, a);
+            default: return SDC_STATUS_UNSUPPORTED;
+        }
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_rollback(const sdc_page_pool_t* pool, const int64_t* clear_slots, int64_t num_clear,
+                                  const sdc_table_edits_t* edits, int32_t* device_status, uintptr_t stream) {
+    try {
+        sdc_status_t rc = validate_pool(pool);
+        if (rc != SDC_STATUS_OK) return rc;
+        TableEdits te;
+        rc = validate_edits(edits, &te);
+        if (rc != SDC_STATUS_OK) return rc;
+        if (device_status == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        if (num_clear < 0) return SDC_STATUS_INVALID_SIZE;
+        if (num_clear > 0 && clear_slots == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        const bool has_edits = te.num_entries > 0 || te.num_lengths > 0;
+        if (num_clear == 0 && !has_edits) return SDC_STATUS_OK;
+        const int lpv = lanes_per_vector(pool->head_dim);
+        RollbackArgs a;
+        a.pool = to_pool(pool);
+        a.slots = clear_slots;
+        a.total_vectors = num_clear * pool->num_layers * 2 * pool->num_heads;
+        a.vector_blocks = vector_blocks(a.total_vectors, lpv);
+        a.edits = te;
+        a.status = device_status;
+        const int64_t blocks = a.vector_blocks + (has_edits ? 1 : 0);
+        if (blocks > INT32_MAX) return SDC_STATUS_OVERFLOW;
+        return launch_rollback(lpv, blocks, as_stream(stream), a);
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_gather_dequantize(const sdc_page_pool_t* pool, int64_t layer_begin, int64_t num_layers,
+                                           const int64_t* slot_mapping, int64_t num_tokens, void* out_keys,
+                                           void* out_values, int out_dtype, int64_t out_token_stride,
+                                           int64_t out_layer_stride, int64_t out_head_stride,
+                                           int32_t* device_status, uintptr_t stream) {
+    try {
+        sdc_status_t rc = validate_pool(pool);
+        if (rc != SDC_STATUS_OK) return rc;
+        if (device_status == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        if (num_tokens < 0 || num_layers < 1) return SDC_STATUS_INVALID_SIZE;
+        if (layer_begin < 0 || layer_begin + num_layers > pool->num_layers) return SDC_STATUS_INVALID_SIZE;
+        if (num_tokens == 0) return SDC_STATUS_OK;
+        if (slot_mapping == nullptr || out_keys == nullptr || out_values == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        const int es = dtype_size(out_dtype);
+        if (es == 0) return SDC_STATUS_UNSUPPORTED;
+        if (out_token_stride < 0 || out_layer_stride < 0 || out_head_stride < 0) return SDC_STATUS_INVALID_SIZE;
+        if (!aligned16(out_keys) || !aligned16(out_values) || (out_token_stride * es) % 16 ||
+            (out_layer_stride * es) % 16 || (out_head_stride * es) % 16) {
+            return SDC_STATUS_MISALIGNED;
+        }
+        const int lpv = lanes_per_vector(pool->head_dim);
+        GatherArgs a;
+        a.pool = to_pool(pool);
+        a.layer_begin = layer_begin;
+        a.num_layers = num_layers;
+        a.slots = slot_mapping;
+        a.total_vectors = num_tokens * num_layers * 2 * pool->num_heads;
+        a.out_keys = out_keys;
+        a.out_values = out_values;
+        a.o_tok = out_token_stride;
+        a.o_layer = out_layer_stride;
+        a.o_head = out_head_stride;
+        a.status = device_status;
+        const int64_t blocks = vector_blocks(a.total_vectors, lpv);
+        if (blocks > INT32_MAX) return SDC_STATUS_OVERFLOW;
+        cudaStream_t st = as_stream(stream);
+        switch (out_dtype) {
+            case SDC_DTYPE_F32: return launch_gather<float>(lpv, blocks, st, a);
+            case SDC_DTYPE_BF16: return launch_gather<__nv_bfloat16>(lpv, blocks, st, a);
+            case SDC_DTYPE_F16: return launch_gather<__half>(lpv, blocks, st, a);
+            case SDC_DTYPE_F64: return launch_gather<double>(lpv, blocks, st, a);
+            default: return SDC_STATUS_UNSUPPORTED;
+        }
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+}  // extern "C"

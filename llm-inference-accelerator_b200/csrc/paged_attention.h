@@ -1,0 +1,38 @@
+// Internal interface between the attention entry point and its kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "sdc_common.cuh"
+
+namespace sdc {
+
+struct AttnArgs {
+    Pool pool;
+    int64_t layer;
+    const void* query;
+    int query_dtype;
+    void* out;
+    int64_t batch;
+    int64_t query_heads;
+    int64_t kv_heads;
+    int64_t group;   // query heads per KV head
+    int64_t window;  // query rows per head (speculative window)
+    int64_t rows;    // group * window: query rows served per KV head
+    int64_t head_dim;
+    const int32_t* block_tables;
+    int64_t table_stride;
+    const int32_t* context_lens;
+    int64_t chunk;       // key positions per work item
+    int64_t max_chunks;  // ceil(max_context_len / chunk)
+    float* part_o;       // [batch * kv_heads][max_chunks][rows][head_dim]
+    float* part_ml;      // [batch * kv_heads][max_chunks][rows][2]
+    int32_t* status;
+    float qk_scale;      // log2(e) / sqrt(head_dim)
+};
+
+bool simt_supports(int64_t head_dim, int64_t rows);
+sdc_status_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream);
+
+}  // namespace sdc

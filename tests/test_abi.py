@@ -1,0 +1,85 @@
+"""The C-ABI library loads and exports what include/specdecode_cuda.h
+declares.  CPU only: these calls validate arguments and return before any
+device work."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from specdecode_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "specdecode_cuda.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"SDC_API\s+[\w\s\*]+?\b(sdc_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load_library()
+
+
+def test_header_declares_the_loader_symbol_list():
+    assert declared_symbols() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in declared_symbols():
+        assert hasattr(lib.handle, name), name
+
+
+def test_no_undeclared_sdc_symbols_are_exported(lib):
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", lib.path], capture_output=True, text=True, check=True)
+    exported = sorted({line.split()[-1] for line in out.stdout.splitlines() if " T sdc_" in line})
+    assert exported == declared_symbols()
+
+
+def test_abi_version_and_status_strings(lib):
+    assert lib.handle.sdc_abi_version() == _lib.ABI_VERSION == 0x00020001
+    assert lib.status_string(0) == "ok"
+    assert lib.status_string(3) == "non-finite value"
+    assert lib.status_string(10) == "invalid quantization scale"
+    assert lib.status_string(999) == "unknown status"
+
+
+def test_host_validation_rejects_before_device_work(lib):
+    h = lib.handle
+    # reference conventions: null arguments and empty vectors are rejected first
+    assert h.sdc_quantize_symmetric_int8_f64(None, 4, None, None) == _lib.STATUS_NULL_ARGUMENT
+    values = (ctypes.c_double * 1)(1.0)
+    out = (ctypes.c_int8 * 1)()
+    scale = ctypes.c_double()
+    assert h.sdc_quantize_symmetric_int8_f64(values, 0, out, ctypes.byref(scale)) == _lib.STATUS_INVALID_SIZE
+    codes = (ctypes.c_int8 * 1)(1)
+    dq = (ctypes.c_double * 1)(8.0)
+    assert h.sdc_dequantize_symmetric_int8_f64(codes, 1, 0.0, dq) == _lib.STATUS_INVALID_SCALE
+    assert dq[0] == 8.0  # untouched on error
+    assert h.sdc_dequantize_symmetric_int8_f64(codes, 1, -1.0, dq) == _lib.STATUS_INVALID_SCALE
+    assert h.sdc_quantize_append(None, 0, 1, None, None, 0, 0, 0, 0, 0, None, None, None, 0) == \
+        _lib.STATUS_NULL_ARGUMENT
+    pool = _lib.PagePool(16, 16, 16, 16, 4, 2, 1, 1, 24, 48, 48, 48, 2, 2, 2)
+    status = ctypes.c_int32()
+    assert h.sdc_rollback(ctypes.byref(pool), None, 0, None, ctypes.byref(status), 0) == _lib.STATUS_UNSUPPORTED
+
+
+def test_workspace_sizing_is_host_only(lib):
+    size = ctypes.c_size_t()
+    assert lib.handle.sdc_paged_attention_workspace_size(32, 32, 8, 128, 5, 8192, ctypes.byref(size)) == 0
+    assert size.value > 0
+    assert lib.handle.sdc_paged_attention_workspace_size(1, 6, 4, 128, 5, 100, ctypes.byref(size)) == \
+        _lib.STATUS_INVALID_ARGUMENT
+    assert lib.handle.sdc_paged_attention_workspace_size(1, 8, 8, 128, 9, 8, ctypes.byref(size)) == \
+        _lib.STATUS_INVALID_SIZE
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(_lib.NativeLibraryNotFound):
+        _lib.load_library(tmp_path / "does-not-exist.so")
