@@ -74,7 +74,8 @@ struct SimtSmem {
 template <typename QT, int D, int RPW>
 __global__ void __launch_bounds__(kThreadsAttn) attn_simt_kernel(AttnArgs a) {
     constexpr int kRow = SimtSmem<D>::kRow;
-    constexpr int DPL = D / 32;  // head_dim elements per lane in the P.V product
+    constexpr int DPL = D >= 32 ? D / 32 : 1;  // head_dim elements per lane in the P.V product
+    const bool pv_lane = lane * DPL < D;        // head_dim < 32 leaves upper lanes idle
     extern __shared__ __align__(16) unsigned char smem[];
     const int R = static_cast<int>(a.rows);
     float* q_s = reinterpret_cast<float*>(smem);
@@ -213,6 +214,7 @@ __global__ void __launch_bounds__(kThreadsAttn) attn_simt_kernel(AttnArgs a) {
         // P.V: lane owns head_dim slice [lane*DPL, lane*DPL + DPL).
 #pragma unroll 4
         for (int tok = 0; tok < kTile; ++tok) {
+            if (!pv_lane) break;
             float vf[DPL];
             const int8_t* vrow = v_s + tok * kRow + lane * DPL;
             if constexpr (DPL == 4) {
@@ -239,8 +241,10 @@ __global__ void __launch_bounds__(kThreadsAttn) attn_simt_kernel(AttnArgs a) {
     for (int j = 0; j < RPW; ++j) {
         const int r = warp + kWarps * j;
         if (r < R) {
+            if (pv_lane) {
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) part_o[r * D + lane * DPL + e] = acc[j][e];
+                for (int e = 0; e < DPL; ++e) part_o[r * D + lane * DPL + e] = acc[j][e];
+            }
             if (lane == 0) {
                 part_ml[2 * r + 0] = m_run[j];
                 part_ml[2 * r + 1] = l_run[j];
@@ -325,6 +329,8 @@ sdc_status_t launch_simt_typed(const AttnArgs& a, cudaStream_t st) {
     dim3 grid(static_cast<unsigned>(a.max_chunks), static_cast<unsigned>(a.batch * a.kv_heads));
     sdc_status_t rc;
     switch (a.head_dim) {
+        case 16: rc = launch_simt_rows<QT, 16>(a, rpw, grid, SimtSmem<16>::bytes(static_cast<int>(a.rows)), st); break;
+        case 32: rc = launch_simt_rows<QT, 32>(a, rpw, grid, SimtSmem<32>::bytes(static_cast<int>(a.rows)), st); break;
         case 64: rc = launch_simt_rows<QT, 64>(a, rpw, grid, SimtSmem<64>::bytes(static_cast<int>(a.rows)), st); break;
         case 128: rc = launch_simt_rows<QT, 128>(a, rpw, grid, SimtSmem<128>::bytes(static_cast<int>(a.rows)), st); break;
         case 256: rc = launch_simt_rows<QT, 256>(a, rpw, grid, SimtSmem<256>::bytes(static_cast<int>(a.rows)), st); break;
@@ -338,7 +344,8 @@ sdc_status_t launch_simt_typed(const AttnArgs& a, cudaStream_t st) {
 }  // namespace
 
 bool simt_supports(int64_t head_dim, int64_t rows) {
-    return (head_dim == 64 || head_dim == 128 || head_dim == 256) && rows >= 1 && rows <= kWarps * 8;
+    return (head_dim == 16 || head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256) && rows >= 1 &&
+           rows <= kWarps * 8;
 }
 
 sdc_status_t launch_attention_simt(const AttnArgs& a, cudaStream_t st) {

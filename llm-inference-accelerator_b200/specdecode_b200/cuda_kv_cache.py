@@ -99,6 +99,7 @@ class PagedVerifyAttention:
         self.library = library
         self.status = status
         self._workspace = None
+        self._sizes: dict[tuple[int, int, int, int], int] = {}
 
     @classmethod
     def for_cache(cls, cache: PagedKVCache) -> "PagedVerifyAttention":
@@ -107,10 +108,14 @@ class PagedVerifyAttention:
     def workspace_bytes(self, batch: int, query_heads: int, window: int, max_context_len: int) -> int:
         import ctypes
 
+        key = (batch, query_heads, window, max_context_len)
+        if key in self._sizes:
+            return self._sizes[key]
         size = ctypes.c_size_t()
         self.library.check(self.library.handle.sdc_paged_attention_workspace_size(
             batch, query_heads, self.pool.num_heads, self.pool.head_dim, window, max_context_len,
             ctypes.byref(size)), "attention workspace sizing")
+        self._sizes[key] = int(size.value)
         return int(size.value)
 
     def __call__(self, query, block_tables, context_lens, max_context_len: int, layer: int, *, out=None):
@@ -203,7 +208,7 @@ class CudaPagedKVCacheStorage:
         length = cache.sequence_length(sequence_id)
         if self._sequence_id is not None and sequence_id != self._sequence_id:
             raise CudaPagedKVCacheError("CUDA paged-cache storage is already bound to another sequence")
-        stable = cache.changes_since(sequence_id, self._tokens) if self._sequence_id is not None else 0
+        stable = cache.changes_since(sequence_id, self._tokens)
         table = cache.block_table(sequence_id)
         bs = self.config.block_size
         new_slots = tuple(table[t // bs] * bs + t % bs for t in range(length))

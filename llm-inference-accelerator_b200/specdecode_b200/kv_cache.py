@@ -33,7 +33,7 @@ from typing import Protocol, runtime_checkable
 import numpy as np
 
 from . import _lib
-from .page_table import AppendPlan, KVCacheCapacityError, KVCacheError, PageTable, TruncatePlan
+from .page_table import AppendPlan, KVCacheCapacityError, KVCacheError, PageTable, TruncatePlan  # noqa: F401
 
 __all__ = [
     "KVCacheError", "KVCacheCapacityError", "KVCacheConfig", "QuantizedVector", "KVQuantizer",
@@ -183,11 +183,12 @@ class _MetadataRing:
     """Pinned host staging + device buffers for per-call metadata (slots,
     table edits, lengths), uploaded with one asynchronous copy.
 
-    ``upload`` fills the next ring slot and enqueues its copy; the caller
-    launches the kernel that reads it and then calls ``release``, which records
-    an event behind that kernel.  A slot is refilled only after its event has
-    completed, so neither its pinned host bytes nor its device bytes are
-    overwritten while a copy or kernel may still read them."""
+    ``upload`` fills the next ring slot, enqueues its copy and returns a
+    ticket; after launching the kernel that reads it, the caller passes the
+    ticket to ``release``, which records an event behind that kernel.  A slot
+    is refilled only after its event has completed, so neither its pinned host
+    bytes nor its device bytes are overwritten while a copy or kernel may still
+    read them."""
 
     def __init__(self, device, depth: int = 4, initial_bytes: int = 1 << 16) -> None:
         torch = _torch()
@@ -196,10 +197,10 @@ class _MetadataRing:
         self.host = [torch.empty(initial_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(depth)]
         self.dev = [torch.empty(initial_bytes, dtype=torch.uint8, device=device) for _ in range(depth)]
         self.events = [None] * depth
+        self.busy = [False] * depth
         self.at = 0
-        self.current = -1
 
-    def upload(self, parts: Sequence[np.ndarray], stream) -> list[int]:
+    def upload(self, parts: Sequence[np.ndarray], stream) -> tuple[list[int], int]:
         torch = _torch()
         sizes = [int(p.nbytes) for p in parts]
         offsets, total = [], 0
@@ -209,6 +210,8 @@ class _MetadataRing:
         total = max(total, 16)
         slot = self.at
         self.at = (self.at + 1) % self.depth
+        if self.busy[slot]:
+            raise RuntimeError("metadata ring overrun: a prepared operation was never committed")
         if self.events[slot] is not None:
             self.events[slot].synchronize()
             self.events[slot] = None
@@ -222,18 +225,41 @@ class _MetadataRing:
                 host[off:off + size] = np.ascontiguousarray(part).view(np.uint8).reshape(-1)
         with torch.cuda.stream(stream):
             self.dev[slot][:total].copy_(self.host[slot][:total], non_blocking=True)
-        self.current = slot
+        self.busy[slot] = True
         base = self.dev[slot].data_ptr()
-        return [base + off for off in offsets]
+        return [base + off for off in offsets], slot
 
-    def release(self, stream) -> None:
+    def release(self, ticket: int, stream) -> None:
         torch = _torch()
-        if self.current < 0:
-            return
         event = torch.cuda.Event()
         event.record(stream)
-        self.events[self.current] = event
-        self.current = -1
+        self.events[ticket] = event
+        self.busy[ticket] = False
+
+
+@dataclass
+class PendingAppend:
+    """A planned append whose metadata is already on its way to the device;
+    ``PagedKVCache.commit_append`` launches it."""
+
+    plan: AppendPlan
+    keys: object
+    values: object
+    layer_begin: int
+    layers: int
+    pointers: list
+    ticket: int
+    stream: object
+
+
+@dataclass
+class PendingTruncate:
+    plan: TruncatePlan
+    pointers: list | None
+    ticket: int
+    stream: object
+    sequence_ids: list
+    counts: list
 
 
 class PagedKVCache:
@@ -374,47 +400,33 @@ class PagedKVCache:
             tensor = tensor.contiguous()
         return tensor
 
-    def _launch_append(self, plan: AppendPlan, keys, values, layer_begin: int, layers: int) -> None:
-        stream = self._stream()
-        slots_ptr, entries_ptr, lengths_ptr = self._meta.upload(
-            [plan.slots, plan.table_entries, plan.new_lengths], stream)
+    def _prepare_append(self, sequence_ids, keys, values, counts, layer_begin: int, layers: int) -> PendingAppend:
+        plan = self._pages.plan_append(sequence_ids, counts)
+        try:
+            stream = self._stream()
+            pointers, ticket = self._meta.upload([plan.slots, plan.table_entries, plan.new_lengths], stream)
+        except Exception:
+            self._pages.undo_append(plan)
+            raise
+        return PendingAppend(plan, keys, values, layer_begin, layers, pointers, ticket, stream)
+
+    def commit_append(self, pending: PendingAppend) -> list[tuple[int, ...]]:
+        """Launch a prepared append; returns the token indices per sequence."""
+        plan, keys, values = pending.plan, pending.keys, pending.values
+        slots_ptr, entries_ptr, lengths_ptr = pending.pointers
         edits = self._edits(entries_ptr, len(plan.table_entries), lengths_ptr, len(plan.new_lengths))
         n = int(plan.slots.size)
         try:
             status = self._lib.handle.sdc_quantize_append(
-                self.pool_desc, layer_begin, layers, keys.data_ptr() if n else None,
+                self.pool_desc, pending.layer_begin, pending.layers, keys.data_ptr() if n else None,
                 values.data_ptr() if n else None, _dtype_code(keys.dtype), n,
                 keys.stride(0), keys.stride(1), keys.stride(2), slots_ptr, edits,
-                self._status.data_ptr(), stream.cuda_stream)
+                self._status.data_ptr(), pending.stream.cuda_stream)
         finally:
-            self._meta.release(stream)
-        self._lib.check(status, "quantize-append")
-
-    def _undo_append(self, plan: AppendPlan) -> None:
-        """Zero the slots an append wrote and rewind the device tables."""
-        stream = self._stream()
-        rewind_entries = plan.table_entries.copy()
-        rewind_entries[:, 2] = -1
-        old_lengths = np.stack([plan.rows, plan.starts], axis=1).astype(np.int32)
-        slots_ptr, entries_ptr, lengths_ptr = self._meta.upload(
-            [plan.slots, rewind_entries, old_lengths], stream)
-        edits = self._edits(entries_ptr, len(rewind_entries), lengths_ptr, len(old_lengths))
-        try:
-            status = self._lib.handle.sdc_rollback(
-                self.pool_desc, slots_ptr, int(plan.slots.size), edits, self._status.data_ptr(),
-                stream.cuda_stream)
-        finally:
-            self._meta.release(stream)
-        self._lib.check(status, "rollback")
-        self._pages.undo_append(plan)
-
-    def _append(self, sequence_ids, keys, values, counts, layer_begin: int, layers: int):
-        plan = self._pages.plan_append(sequence_ids, counts)
-        try:
-            self._launch_append(plan, keys, values, layer_begin, layers)
-        except Exception:
+            self._meta.release(pending.ticket, pending.stream)
+        if status != _lib.STATUS_OK:
             self._pages.undo_append(plan)
-            raise
+            self._lib.check(status, "quantize-append")
         if self.check_status_after_each_call:
             bits = self.status_bits()
             if bits:
@@ -426,7 +438,25 @@ class PagedKVCache:
                     raise ValueError("quantization scale is outside the float32 range")
                 raise _lib.NativeBackendError(f"device fault: {_lib.fault_message(bits)}",
                                               status=_lib.STATUS_DEVICE_FAULT, faults=bits)
-        return plan
+        return [tuple(range(int(s), int(s) + int(c))) for s, c in zip(plan.starts, plan.counts)]
+
+    def _undo_append(self, plan: AppendPlan) -> None:
+        """Zero the slots an append wrote and rewind the device tables."""
+        stream = self._stream()
+        rewind_entries = plan.table_entries.copy()
+        rewind_entries[:, 2] = -1
+        old_lengths = np.stack([plan.rows, plan.starts], axis=1).astype(np.int32)
+        (slots_ptr, entries_ptr, lengths_ptr), ticket = self._meta.upload(
+            [plan.slots, rewind_entries, old_lengths], stream)
+        edits = self._edits(entries_ptr, len(rewind_entries), lengths_ptr, len(old_lengths))
+        try:
+            status = self._lib.handle.sdc_rollback(
+                self.pool_desc, slots_ptr, int(plan.slots.size), edits, self._status.data_ptr(),
+                stream.cuda_stream)
+        finally:
+            self._meta.release(ticket, stream)
+        self._lib.check(status, "rollback")
+        self._pages.undo_append(plan)
 
     def append_tensor(self, sequence_id: Hashable, keys, values) -> tuple[int, ...]:
         """Atomically quantize and append ``keys``/``values`` of shape
@@ -443,13 +473,14 @@ class PagedKVCache:
         n = int(keys.shape[0])
         if n == 0:
             return ()
-        plan = self._append([sequence_id], keys, values, [n], 0, L)
-        start = int(plan.starts[0])
-        return tuple(range(start, start + n))
+        return self.commit_append(self._prepare_append([sequence_id], keys, values, [n], 0, L))[0]
 
-    def append_batch(self, sequence_ids: Sequence[Hashable], keys, values) -> list[tuple[int, ...]]:
-        """Append ``keys``/``values`` ``[batch, tokens, layers, heads, dim]`` —
-        the same number of tokens to every listed sequence — in one launch."""
+    def prepare_append_batch(self, sequence_ids: Sequence[Hashable], keys, values) -> PendingAppend:
+        """Validate and plan an append of ``keys``/``values``
+        ``[batch, tokens, layers, heads, dim]`` — the same number of tokens to
+        every listed sequence — and stage its metadata; ``commit_append``
+        launches it.  Allocation state changes here; a prepared append must be
+        committed before the next one is prepared."""
         if keys.dim() != 5 or values.shape != keys.shape:
             raise ValueError("keys/values must have shape [batch, tokens, layers, heads, dim]")
         B, n = int(keys.shape[0]), int(keys.shape[1])
@@ -460,8 +491,11 @@ class PagedKVCache:
         flat_v = self._as_kv_tensor(values.reshape(B * n, *values.shape[2:]), "values", L)
         if flat_v.dtype != flat_k.dtype:
             flat_v = flat_v.to(flat_k.dtype)
-        plan = self._append(list(sequence_ids), flat_k, flat_v, [n] * B, 0, L)
-        return [tuple(range(int(s), int(s) + n)) for s in plan.starts]
+        return self._prepare_append(list(sequence_ids), flat_k, flat_v, [n] * B, 0, L)
+
+    def append_batch(self, sequence_ids: Sequence[Hashable], keys, values) -> list[tuple[int, ...]]:
+        """Append to many sequences in one launch (see ``prepare_append_batch``)."""
+        return self.commit_append(self.prepare_append_batch(sequence_ids, keys, values))
 
     def append(self, sequence_id: Hashable, keys, values) -> int:
         return self.append_many(sequence_id, ((keys, values),))[0]
@@ -509,35 +543,40 @@ class PagedKVCache:
         return host.pin_memory().to(self.device, non_blocking=True)
 
     # -- rollback ---------------------------------------------------------------
-    def _launch_truncate(self, plan: TruncatePlan) -> None:
-        if plan.cleared_slots.size == 0 and plan.table_entries.size == 0:
-            return  # nothing discarded: lengths are unchanged
+    def prepare_truncate_batch(self, sequence_ids: Sequence[Hashable], token_counts) -> PendingTruncate:
+        """Plan a rollback of several sequences and stage its metadata;
+        ``commit_truncate`` launches it."""
+        sequence_ids, counts = list(sequence_ids), list(token_counts)
+        plan = self._pages.plan_truncate(sequence_ids, counts)
         stream = self._stream()
-        slots_ptr, entries_ptr, lengths_ptr = self._meta.upload(
-            [plan.cleared_slots, plan.table_entries, plan.new_lengths], stream)
-        edits = self._edits(entries_ptr, len(plan.table_entries), lengths_ptr, len(plan.new_lengths))
-        try:
-            status = self._lib.handle.sdc_rollback(
-                self.pool_desc, slots_ptr, int(plan.cleared_slots.size), edits, self._status.data_ptr(),
-                stream.cuda_stream)
-        finally:
-            self._meta.release(stream)
-        self._lib.check(status, "rollback")
+        if plan.cleared_slots.size == 0 and plan.table_entries.size == 0:
+            return PendingTruncate(plan, None, -1, stream, sequence_ids, counts)
+        pointers, ticket = self._meta.upload([plan.cleared_slots, plan.table_entries, plan.new_lengths], stream)
+        return PendingTruncate(plan, pointers, ticket, stream, sequence_ids, counts)
+
+    def commit_truncate(self, pending: PendingTruncate) -> list[int]:
+        plan = pending.plan
+        if pending.pointers is not None:  # otherwise nothing was discarded
+            slots_ptr, entries_ptr, lengths_ptr = pending.pointers
+            edits = self._edits(entries_ptr, len(plan.table_entries), lengths_ptr, len(plan.new_lengths))
+            try:
+                status = self._lib.handle.sdc_rollback(
+                    self.pool_desc, slots_ptr, int(plan.cleared_slots.size), edits, self._status.data_ptr(),
+                    pending.stream.cuda_stream)
+            finally:
+                self._meta.release(pending.ticket, pending.stream)
+            self._lib.check(status, "rollback")
+        for seq, count in zip(pending.sequence_ids, pending.counts):
+            self._low_water[seq] = min(self._low_water.get(seq, int(count)), int(count))
+        return [int(r) for r in plan.released]
 
     def truncate(self, sequence_id: Hashable, token_count: int) -> int:
         """Discard a suffix; returns the number of physical blocks released
         (kv_cache.py:395-420)."""
-        plan = self._pages.plan_truncate([sequence_id], [token_count])
-        self._launch_truncate(plan)
-        self._low_water[sequence_id] = min(self._low_water.get(sequence_id, int(token_count)), int(token_count))
-        return int(plan.released[0])
+        return self.commit_truncate(self.prepare_truncate_batch([sequence_id], [token_count]))[0]
 
     def truncate_batch(self, sequence_ids: Sequence[Hashable], token_counts) -> list[int]:
-        plan = self._pages.plan_truncate(list(sequence_ids), list(token_counts))
-        self._launch_truncate(plan)
-        for seq, count in zip(sequence_ids, token_counts):
-            self._low_water[seq] = min(self._low_water.get(seq, int(count)), int(count))
-        return [int(r) for r in plan.released]
+        return self.commit_truncate(self.prepare_truncate_batch(sequence_ids, token_counts))
 
     def checkpoint(self, sequence_id: Hashable) -> KVCacheCheckpoint:
         return KVCacheCheckpoint(sequence_id, self.sequence_length(sequence_id))
@@ -566,14 +605,14 @@ class PagedKVCache:
         if n == 0:
             return out_k, out_v
         stream = self._stream()
-        (slots_ptr,) = self._meta.upload([slots.astype(np.int64)], stream)
+        (slots_ptr,), ticket = self._meta.upload([slots.astype(np.int64)], stream)
         try:
             status = self._lib.handle.sdc_gather_dequantize(
                 self.pool_desc, layer_begin, layers, slots_ptr, n, out_k.data_ptr(), out_v.data_ptr(),
                 _dtype_code(dtype), out_k.stride(0), out_k.stride(1), out_k.stride(2),
                 self._status.data_ptr(), stream.cuda_stream)
         finally:
-            self._meta.release(stream)
+            self._meta.release(ticket, stream)
         self._lib.check(status, "gather-dequantize")
         return out_k, out_v
 
