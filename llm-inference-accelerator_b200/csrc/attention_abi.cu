@@ -15,13 +15,17 @@ struct Plan {
     int64_t rows;
     int64_t chunk;
     int64_t max_chunks;
+    bool tensor_cores;  // shape served by the tcgen05 item kernel
     size_t part_o_bytes;
     size_t part_ml_bytes;
+    size_t extra_bytes;
     size_t total;
 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Work planning depends on the shape only, so the workspace sized here fits
+// whichever item kernel the pool layout selects at launch.
 sdc_status_t make_plan(int64_t batch, int64_t hq, int64_t hkv, int64_t d, int64_t window, int64_t max_ctx,
                        Plan* p) {
     if (batch < 1 || hq < 1 || hkv < 1 || d < 1 || window < 1 || max_ctx < 1) return SDC_STATUS_INVALID_SIZE;
@@ -29,13 +33,15 @@ sdc_status_t make_plan(int64_t batch, int64_t hq, int64_t hkv, int64_t d, int64_
     if (window > max_ctx) return SDC_STATUS_INVALID_SIZE;
     p->rows = (hq / hkv) * window;
     if (!simt_supports(d, p->rows)) return SDC_STATUS_UNSUPPORTED;
-    p->chunk = kSimtChunk;
+    p->tensor_cores = tc::shape_supported(d, p->rows);
+    p->chunk = p->tensor_cores ? tc::chunk_for(batch, hkv, max_ctx) : kSimtChunk;
     p->max_chunks = ceil_div(max_ctx, p->chunk);
     const double items = static_cast<double>(batch) * hkv * p->max_chunks;
     if (items * p->rows * (d + 2) * 4.0 > 9.0e18) return SDC_STATUS_OVERFLOW;
     p->part_o_bytes = align_up(static_cast<size_t>(batch * hkv * p->max_chunks * p->rows * d) * 4, 256);
     p->part_ml_bytes = align_up(static_cast<size_t>(batch * hkv * p->max_chunks * p->rows * 2) * 4, 256);
-    p->total = p->part_o_bytes + p->part_ml_bytes;
+    p->extra_bytes = p->tensor_cores ? align_up(tc::extra_workspace(batch, hkv, p->max_chunks, p->rows), 256) : 0;
+    p->total = p->part_o_bytes + p->part_ml_bytes + p->extra_bytes;
     return SDC_STATUS_OK;
 }
 
@@ -109,6 +115,10 @@ SDC_API sdc_status_t sdc_paged_verify_attention(const sdc_page_pool_t* pool, int
         a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.part_o_bytes);
         a.status = device_status;
         a.qk_scale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(pool->head_dim)));
+        if (p.tensor_cores && tc::supports(a)) {
+            void* extra = static_cast<char*>(workspace) + p.part_o_bytes + p.part_ml_bytes;
+            return tc::launch(a, extra, as_stream(stream));
+        }
         return launch_attention_simt(a, as_stream(stream));
     } catch (...) {
         return SDC_STATUS_INTERNAL_ERROR;

@@ -31,14 +31,52 @@ struct AccOf<double> {
 __device__ __forceinline__ float amax(float a, float b) { return fmaxf(a, b); }
 __device__ __forceinline__ double amax(double a, double b) { return fmax(a, b); }
 
+// max that propagates NaN, so one reduction finds both the vector maximum and
+// any non-finite element (the result is then NaN or +inf).
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
 template <typename Src>
-__device__ __forceinline__ int quant_one(typename AccOf<Src>::type x, float s) {
+__device__ __forceinline__ int quant_one(typename AccOf<Src>::type x, float s, float rcp) {
     if constexpr (std::is_same<Src, double>::value) {
         return quant_code_f64(x, static_cast<double>(s));
     } else {
-        return s >= kFloatPathMinScale ? quant_code_f32(x, s)
+        return s >= kFloatPathMinScale ? quant_code_f32(x, s, rcp)
                                        : quant_code_f64(static_cast<double>(x), static_cast<double>(s));
     }
+}
+
+// Per-group maximum of |x| over 16 elements per lane and LPV lanes; for float
+// sources a non-finite element makes the result NaN or +inf.
+template <typename Src, int LPV>
+__device__ __forceinline__ typename AccOf<Src>::type group_absmax(const typename AccOf<Src>::type (&x)[16],
+                                                                  int& bad) {
+    using Acc = typename AccOf<Src>::type;
+    Acc m = Acc(0);
+    if constexpr (std::is_same<Src, double>::value) {
+        int b = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            b |= !isfinite(x[i]);
+            m = fmax(m, fabs(x[i]));
+        }
+#pragma unroll
+        for (int off = LPV / 2; off > 0; off >>= 1) {
+            m = fmax(m, __shfl_xor_sync(kFullMask, m, off));
+            b |= __shfl_xor_sync(kFullMask, b, off);
+        }
+        bad = b;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) m = max_nan(m, fabsf(x[i]));
+#pragma unroll
+        for (int off = LPV / 2; off > 0; off >>= 1) m = max_nan(m, __shfl_xor_sync(kFullMask, m, off));
+        bad = !(m < INFINITY);
+    }
+    return m;
 }
 
 struct AppendArgs {
@@ -49,8 +87,11 @@ struct AppendArgs {
     int64_t num_src_layers;
     int64_t s_tok, s_layer, s_head;
     const int64_t* slots;
-    int64_t total_vectors;
-    int64_t vector_blocks;
+    uint32_t total_vectors;
+    uint32_t vector_blocks;
+    FastDiv div_heads;   // num_heads
+    FastDiv div_layers;  // num_src_layers
+    FastDiv div_block;   // block_size
     TableEdits edits;
     int32_t* status;
 };
@@ -63,22 +104,19 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
         return;
     }
     constexpr int VPW = 32 / LPV;
-    const int lane = threadIdx.x & 31;
-    const int sub = lane & (LPV - 1);
-    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t v = warp * VPW + lane / LPV;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t sub = lane & (LPV - 1);
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t v = warp * VPW + lane / LPV;
     const bool active = v < a.total_vectors;
-    const int64_t H = a.pool.num_heads;
-    const int64_t D = a.pool.head_dim;
+    const uint32_t D = static_cast<uint32_t>(a.pool.head_dim);
 
-    int64_t head = 0, kv = 0, layer_rel = 0, token = 0;
+    uint32_t head = 0, kv = 0, layer_rel = 0, token = 0;
     if (active) {
-        head = v % H;
-        int64_t r = v / H;
+        uint32_t r;
+        a.div_heads.divmod(v, r, head);
         kv = r & 1;
-        r >>= 1;
-        layer_rel = r % a.num_src_layers;
-        token = r / a.num_src_layers;
+        a.div_layers.divmod(r >> 1, token, layer_rel);
     }
     const bool has_chunk = active && (sub * 16 < D);
 
@@ -92,17 +130,7 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
         for (int i = 0; i < 16; ++i) x[i] = Acc(0);
     }
     int bad = 0;
-    Acc m = Acc(0);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        bad |= !isfinite(x[i]);
-        m = amax(m, fabs(x[i]));
-    }
-#pragma unroll
-    for (int off = LPV / 2; off > 0; off >>= 1) {
-        m = amax(m, __shfl_xor_sync(kFullMask, m, off));
-        bad |= __shfl_xor_sync(kFullMask, bad, off);
-    }
+    const Acc m = group_absmax<Src, LPV>(x, bad);
     if (!active) return;
 
     const int64_t slot = __ldg(a.slots + token);
@@ -114,8 +142,8 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
         if (sub == 0) report_fault(a.status, SDC_FAULT_NONFINITE_VALUE);
         return;
     }
-    const int64_t blk = slot / a.pool.block_size;
-    const int64_t off = slot - blk * a.pool.block_size;
+    uint32_t blk, off;
+    a.div_block.divmod(static_cast<uint32_t>(slot), blk, off);
     const int64_t layer = a.layer_begin + layer_rel;
     int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
                     head * a.pool.chs + off * D;
@@ -130,9 +158,10 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
             if (sub == 0) report_fault(a.status, SDC_FAULT_INVALID_SCALE);
             return;
         }
+        const float rcp = 1.0f / s;
         int q[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) q[i] = quant_one<Src>(x[i], s);
+        for (int i = 0; i < 16; ++i) q[i] = quant_one<Src>(x[i], s, rcp);
         packed.x = pack4(q[0], q[1], q[2], q[3]);
         packed.y = pack4(q[4], q[5], q[6], q[7]);
         packed.z = pack4(q[8], q[9], q[10], q[11]);
@@ -183,8 +212,9 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const Src* src, int6
         if (lane == 0) row_status[row] = SDC_STATUS_INVALID_SCALE;
         return;
     }
+    const float rcp = 1.0f / s;
     for (int64_t i = lane; i < count; i += 32) {
-        out[i] = static_cast<int8_t>(quant_one<Src>(static_cast<Acc>(x[i]), s));
+        out[i] = static_cast<int8_t>(quant_one<Src>(static_cast<Acc>(x[i]), s, rcp));
     }
     if (lane == 0) {
         scales[row] = s;
@@ -200,8 +230,11 @@ __global__ void dequantize_vector_kernel(const int8_t* codes, int64_t count, dou
 struct RollbackArgs {
     Pool pool;
     const int64_t* slots;
-    int64_t total_vectors;
-    int64_t vector_blocks;
+    uint32_t total_vectors;
+    uint32_t vector_blocks;
+    FastDiv div_heads;
+    FastDiv div_layers;
+    FastDiv div_block;
     TableEdits edits;
     int32_t* status;
 };
@@ -213,26 +246,23 @@ __global__ void __launch_bounds__(256) rollback_kernel(RollbackArgs a) {
         return;
     }
     constexpr int VPW = 32 / LPV;
-    const int lane = threadIdx.x & 31;
-    const int sub = lane & (LPV - 1);
-    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t v = warp * VPW + lane / LPV;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t sub = lane & (LPV - 1);
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t v = warp * VPW + lane / LPV;
     if (v >= a.total_vectors) return;
-    const int64_t H = a.pool.num_heads;
-    const int64_t D = a.pool.head_dim;
-    const int64_t head = v % H;
-    int64_t r = v / H;
-    const int64_t kv = r & 1;
-    r >>= 1;
-    const int64_t layer = r % a.pool.num_layers;
-    const int64_t index = r / a.pool.num_layers;
+    const uint32_t D = static_cast<uint32_t>(a.pool.head_dim);
+    uint32_t r, head, index, layer;
+    a.div_heads.divmod(v, r, head);
+    const uint32_t kv = r & 1;
+    a.div_layers.divmod(r >> 1, index, layer);
     const int64_t slot = __ldg(a.slots + index);
     if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
         if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
         return;
     }
-    const int64_t blk = slot / a.pool.block_size;
-    const int64_t off = slot - blk * a.pool.block_size;
+    uint32_t blk, off;
+    a.div_block.divmod(static_cast<uint32_t>(slot), blk, off);
     if (sub * 16 < D) {
         int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
                         head * a.pool.chs + off * D + sub * 16;
@@ -250,7 +280,10 @@ struct GatherArgs {
     int64_t layer_begin;
     int64_t num_layers;
     const int64_t* slots;
-    int64_t total_vectors;
+    uint32_t total_vectors;
+    FastDiv div_heads;
+    FastDiv div_layers;
+    FastDiv div_block;
     void* out_keys;
     void* out_values;
     int64_t o_tok, o_layer, o_head;
@@ -299,27 +332,24 @@ __device__ __forceinline__ void store16(__half* p, const int (&q)[16], float s) 
 template <typename Out, int LPV>
 __global__ void __launch_bounds__(256) gather_dequantize_kernel(GatherArgs a) {
     constexpr int VPW = 32 / LPV;
-    const int lane = threadIdx.x & 31;
-    const int sub = lane & (LPV - 1);
-    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t v = warp * VPW + lane / LPV;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t sub = lane & (LPV - 1);
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t v = warp * VPW + lane / LPV;
     if (v >= a.total_vectors) return;
-    const int64_t H = a.pool.num_heads;
-    const int64_t D = a.pool.head_dim;
-    const int64_t head = v % H;
-    int64_t r = v / H;
-    const int64_t kv = r & 1;
-    r >>= 1;
-    const int64_t layer_rel = r % a.num_layers;
-    const int64_t token = r / a.num_layers;
+    const uint32_t D = static_cast<uint32_t>(a.pool.head_dim);
+    uint32_t r, head, token, layer_rel;
+    a.div_heads.divmod(v, r, head);
+    const uint32_t kv = r & 1;
+    a.div_layers.divmod(r >> 1, token, layer_rel);
     const int64_t slot = __ldg(a.slots + token);
     if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
         if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
         return;
     }
     if (sub * 16 >= D) return;
-    const int64_t blk = slot / a.pool.block_size;
-    const int64_t off = slot - blk * a.pool.block_size;
+    uint32_t blk, off;
+    a.div_block.divmod(static_cast<uint32_t>(slot), blk, off);
     const int64_t layer = a.layer_begin + layer_rel;
     const int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
                           head * a.pool.chs + off * D + sub * 16;
@@ -578,12 +608,18 @@ SDC_API sdc_status_t sdc_quantize_append(const sdc_page_pool_t* pool, int64_t la
         a.s_layer = src_layer_stride;
         a.s_head = src_head_stride;
         a.slots = slot_mapping;
-        a.total_vectors = num_tokens * num_src_layers * 2 * pool->num_heads;
-        a.vector_blocks = vector_blocks(a.total_vectors, lpv);
+        const int64_t vectors = num_tokens * num_src_layers * 2 * pool->num_heads;
+        const int64_t nblocks = vector_blocks(vectors, lpv);
+        if (vectors >= INT32_MAX || nblocks + 1 >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        if (pool->num_blocks * pool->block_size >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        a.total_vectors = static_cast<uint32_t>(vectors);
+        a.vector_blocks = static_cast<uint32_t>(nblocks);
+        a.div_heads = FastDiv(static_cast<uint32_t>(pool->num_heads));
+        a.div_layers = FastDiv(static_cast<uint32_t>(num_src_layers));
+        a.div_block = FastDiv(static_cast<uint32_t>(pool->block_size));
         a.edits = te;
         a.status = device_status;
-        const int64_t blocks = a.vector_blocks + (has_edits ? 1 : 0);
-        if (blocks > INT32_MAX) return SDC_STATUS_OVERFLOW;
+        const int64_t blocks = nblocks + (has_edits ? 1 : 0);
         cudaStream_t st = as_stream(stream);
         switch (src_dtype) {
             case SDC_DTYPE_F32: return launch_append<float>(lpv, blocks, st, a);
@@ -614,12 +650,18 @@ SDC_API sdc_status_t sdc_rollback(const sdc_page_pool_t* pool, const int64_t* cl
         RollbackArgs a;
         a.pool = to_pool(pool);
         a.slots = clear_slots;
-        a.total_vectors = num_clear * pool->num_layers * 2 * pool->num_heads;
-        a.vector_blocks = vector_blocks(a.total_vectors, lpv);
+        const int64_t vectors = num_clear * pool->num_layers * 2 * pool->num_heads;
+        const int64_t nblocks = vector_blocks(vectors, lpv);
+        if (vectors >= INT32_MAX || nblocks + 1 >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        if (pool->num_blocks * pool->block_size >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        a.total_vectors = static_cast<uint32_t>(vectors);
+        a.vector_blocks = static_cast<uint32_t>(nblocks);
+        a.div_heads = FastDiv(static_cast<uint32_t>(pool->num_heads));
+        a.div_layers = FastDiv(static_cast<uint32_t>(pool->num_layers));
+        a.div_block = FastDiv(static_cast<uint32_t>(pool->block_size));
         a.edits = te;
         a.status = device_status;
-        const int64_t blocks = a.vector_blocks + (has_edits ? 1 : 0);
-        if (blocks > INT32_MAX) return SDC_STATUS_OVERFLOW;
+        const int64_t blocks = nblocks + (has_edits ? 1 : 0);
         return launch_rollback(lpv, blocks, as_stream(stream), a);
     } catch (...) {
         return SDC_STATUS_INTERNAL_ERROR;
@@ -652,15 +694,20 @@ SDC_API sdc_status_t sdc_gather_dequantize(const sdc_page_pool_t* pool, int64_t 
         a.layer_begin = layer_begin;
         a.num_layers = num_layers;
         a.slots = slot_mapping;
-        a.total_vectors = num_tokens * num_layers * 2 * pool->num_heads;
+        const int64_t vectors = num_tokens * num_layers * 2 * pool->num_heads;
+        if (vectors >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        if (pool->num_blocks * pool->block_size >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        a.total_vectors = static_cast<uint32_t>(vectors);
+        a.div_heads = FastDiv(static_cast<uint32_t>(pool->num_heads));
+        a.div_layers = FastDiv(static_cast<uint32_t>(num_layers));
+        a.div_block = FastDiv(static_cast<uint32_t>(pool->block_size));
         a.out_keys = out_keys;
         a.out_values = out_values;
         a.o_tok = out_token_stride;
         a.o_layer = out_layer_stride;
         a.o_head = out_head_stride;
         a.status = device_status;
-        const int64_t blocks = vector_blocks(a.total_vectors, lpv);
-        if (blocks > INT32_MAX) return SDC_STATUS_OVERFLOW;
+        const int64_t blocks = vector_blocks(vectors, lpv);
         cudaStream_t st = as_stream(stream);
         switch (out_dtype) {
             case SDC_DTYPE_F32: return launch_gather<float>(lpv, blocks, st, a);

@@ -75,7 +75,6 @@ template <typename QT, int D, int RPW>
 __global__ void __launch_bounds__(kThreadsAttn) attn_simt_kernel(AttnArgs a) {
     constexpr int kRow = SimtSmem<D>::kRow;
     constexpr int DPL = D >= 32 ? D / 32 : 1;  // head_dim elements per lane in the P.V product
-    const bool pv_lane = lane * DPL < D;        // head_dim < 32 leaves upper lanes idle
     extern __shared__ __align__(16) unsigned char smem[];
     const int R = static_cast<int>(a.rows);
     float* q_s = reinterpret_cast<float*>(smem);
@@ -88,6 +87,7 @@ __global__ void __launch_bounds__(kThreadsAttn) attn_simt_kernel(AttnArgs a) {
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
+    const bool pv_lane = lane * DPL < D;  // head_dim < 32 leaves upper lanes idle in P.V
     const int64_t item = blockIdx.y;  // b * Hkv + h
     const int64_t b = item / a.kv_heads;
     const int64_t h = item - b * a.kv_heads;
@@ -341,11 +341,26 @@ sdc_status_t launch_simt_typed(const AttnArgs& a, cudaStream_t st) {
     return launch_status();
 }
 
+template <typename QT>
+sdc_status_t launch_combine_typed(const AttnArgs& a, cudaStream_t st) {
+    attn_combine_kernel<QT><<<static_cast<unsigned>(a.batch * a.kv_heads), 128, 0, st>>>(a);
+    return launch_status();
+}
+
 }  // namespace
 
 bool simt_supports(int64_t head_dim, int64_t rows) {
     return (head_dim == 16 || head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256) && rows >= 1 &&
            rows <= kWarps * 8;
+}
+
+sdc_status_t launch_attention_combine(const AttnArgs& a, cudaStream_t st) {
+    switch (a.query_dtype) {
+        case SDC_DTYPE_BF16: return launch_combine_typed<__nv_bfloat16>(a, st);
+        case SDC_DTYPE_F16: return launch_combine_typed<__half>(a, st);
+        case SDC_DTYPE_F32: return launch_combine_typed<float>(a, st);
+        default: return SDC_STATUS_UNSUPPORTED;
+    }
 }
 
 sdc_status_t launch_attention_simt(const AttnArgs& a, cudaStream_t st) {

@@ -38,6 +38,32 @@ __device__ __forceinline__ void report_fault(int32_t* status, int32_t bits) {
     if (status != nullptr) atomicOr(status, bits);
 }
 
+// Unsigned 32-bit division by a run-time constant (Granlund-Montgomery):
+// q = (t + ((n - t) >> 1)) >> (shift - 1) with t = umulhi(n, mul).  Exact
+// for every 32-bit n and divisor >= 1.
+struct FastDiv {
+    uint32_t divisor;
+    uint32_t mul;
+    uint32_t shift;
+
+    FastDiv() = default;
+    __host__ explicit FastDiv(uint32_t d) : divisor(d) {
+        uint32_t l = 0;
+        while ((uint64_t(1) << l) < d) ++l;
+        shift = l;
+        mul = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        if (shift == 0) return n;  // divisor 1
+        const uint32_t t = __umulhi(n, mul);
+        return (t + ((n - t) >> 1)) >> (shift - 1);
+    }
+    __device__ __forceinline__ void divmod(uint32_t n, uint32_t& q, uint32_t& r) const {
+        q = div(n);
+        r = n - q * divisor;
+    }
+};
+
 // Loads 16 consecutive source elements (16-byte aligned) as Acc values.
 __device__ __forceinline__ void load16(const float* p, float (&x)[16]) {
     const float4* q = reinterpret_cast<const float4*>(p);
@@ -110,23 +136,25 @@ __device__ __forceinline__ int quant_code_f64(double x, double scale) {
 
 // Float path for inputs that are float32 values (f32 / bf16 / f16 sources).
 // Returns round_half_away(x / s) of the *exact* quotient using only float
-// arithmetic: a candidate from the rounded quotient is corrected by the signs
-// of a - (n +/- 1/2) s, each computed with one fused multiply-add.  Those signs
-// are exact whenever s >= 2^-100 (the residual is a non-zero multiple of at
-// least 2^-149 or exactly zero, so rounding cannot flush it to zero).  For a
-// quotient of two float32 values the double-rounded quotient the reference
-// rounds lands on the same integer as the exact one, because such a quotient
-// is never within 2^-26 of a half-integer without being one.
-__device__ __forceinline__ int quant_code_f32(float x, float s) {
-    const float a = fabsf(x);
-    float n = floorf(__fdiv_rn(a, s) + 0.5f);
-    if (__fmaf_rn(-(n + 0.5f), s, a) >= 0.0f) {
-        n += 1.0f;
-    } else if (__fmaf_rn(-(n - 0.5f), s, a) < 0.0f) {
-        n -= 1.0f;
-    }
-    n = fminf(n, 127.0f);
-    const int q = static_cast<int>(n);
+// arithmetic.  A candidate n0 = rint(|x| * rcp) is within one of the answer
+// (rcp = 1/s rounded once, so |x|*rcp is within 2^-22 relative of |x|/s).  It
+// is corrected by the signs of |x| - (n0 + 1/2) s and |x| - (n0 - 1/2) s,
+// each computed with one fused multiply-add: a correctly rounded result has
+// the sign of the exact residual, and the residual cannot round to zero
+// because it is zero or a multiple of at least 2^-149 (true whenever
+// s >= 2^-100; smaller scales take the double path).  For a quotient of two
+// float32 values the double-rounded quotient the reference rounds lands on
+// the same integer as the exact one, because such a quotient is never within
+// 2^-26 of a half-integer without being one.
+__device__ __forceinline__ float quant_mag_f32(float a, float s, float rcp) {
+    float n = rintf(a * rcp);
+    n += (__fmaf_rn(-(n + 0.5f), s, a) >= 0.0f) ? 1.0f : 0.0f;
+    n -= (__fmaf_rn(-(n - 0.5f), s, a) < 0.0f) ? 1.0f : 0.0f;
+    return fminf(n, 127.0f);
+}
+
+__device__ __forceinline__ int quant_code_f32(float x, float s, float rcp) {
+    const int q = static_cast<int>(quant_mag_f32(fabsf(x), s, rcp));
     return x < 0.0f ? -q : q;
 }
 
