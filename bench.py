@@ -53,6 +53,9 @@ def parse_args(argv=None):
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--skip-append", action="store_true", help="measure only the verify attention")
     p.add_argument("--skip-cpu-baseline", action="store_true")
+    p.add_argument("--profile", action="store_true",
+                   help="verify attention only: no clock sampling, sustained load, host-buffer pass, append "
+                        "workload or CPU baseline (a short, repeatable run for ncu)")
     return p.parse_args(argv)
 
 
@@ -472,6 +475,14 @@ def main(argv=None) -> int:
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
     state = build_verify(args.seed + 1000 * rank, device)
 
+    if args.profile:
+        t_ms, _, _, _ = time_verify(state, args.steps, args.warmup, world, flush)
+        if state["cache"].status_bits():
+            raise RuntimeError("device fault in the verify benchmark")
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "ms_per_step": t_ms / args.steps,
+                              "gbs": state["bytes"] / (t_ms / args.steps / 1e3) / 1e9}))
+        return 0
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler is not None:
         sampler.start()
