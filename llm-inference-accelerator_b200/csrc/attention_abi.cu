@@ -36,6 +36,7 @@ sdc_status_t make_plan(int64_t batch, int64_t hq, int64_t hkv, int64_t d, int64_
     p->tensor_cores = tc::shape_supported(d, p->rows);
     p->chunk = p->tensor_cores ? tc::chunk_for(batch, hkv, max_ctx) : kSimtChunk;
     p->max_chunks = ceil_div(max_ctx, p->chunk);
+    if (!combine_fits(p->max_chunks, p->rows)) return SDC_STATUS_UNSUPPORTED;
     const double items = static_cast<double>(batch) * hkv * p->max_chunks;
     if (items * p->rows * (d + 2) * 4.0 > 9.0e18) return SDC_STATUS_OVERFLOW;
     p->part_o_bytes = align_up(static_cast<size_t>(batch * hkv * p->max_chunks * p->rows * d) * 4, 256);

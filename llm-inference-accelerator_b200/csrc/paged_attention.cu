@@ -263,8 +263,14 @@ template <>
 __device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
 
 // Merges the chunk partials of one (sequence, KV head) and writes the output.
+// Row weights exp2(m_c - m) / L are computed once per (chunk, row) into shared
+// memory; the head_dim sweep is then one coalesced load and FMA per chunk.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineMaxWeights = 12 * 1024;  // 48 KiB of float weights
+
 template <typename QT>
-__global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(AttnArgs a) {
+    __shared__ float weights[kCombineMaxWeights];
     const int64_t item = blockIdx.x;
     const int64_t b = item / a.kv_heads;
     const int64_t h = item - b * a.kv_heads;
@@ -281,19 +287,26 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnArgs a) {
     const int64_t chunks = (T + a.chunk - 1) / a.chunk;
     const float* ml = a.part_ml + item * a.max_chunks * R * 2;
     const float* po = a.part_o + item * a.max_chunks * R * D;
-    for (int64_t idx = threadIdx.x; idx < R * D; idx += blockDim.x) {
-        const int64_t r = idx / D;
+    // the host keeps chunks * rows within the weight buffer
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
         float m = -INFINITY;
         for (int64_t c = 0; c < chunks; ++c) m = fmaxf(m, ml[(c * R + r) * 2]);
-        float l = 0.0f, o = 0.0f;
+        float l = 0.0f;
         for (int64_t c = 0; c < chunks; ++c) {
             const float mc = ml[(c * R + r) * 2];
-            if (mc == -INFINITY) continue;
-            const float w = exp2f(mc - m);
+            const float w = mc == -INFINITY ? 0.0f : exp2f(mc - m);
+            weights[c * R + r] = w;
             l = fmaf(ml[(c * R + r) * 2 + 1], w, l);
-            o = fmaf(po[c * R * D + idx], w, o);
         }
-        out[idx] = from_float<QT>(o / l);
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        for (int64_t c = 0; c < chunks; ++c) weights[c * R + r] *= inv;
+    }
+    __syncthreads();
+    for (int64_t idx = threadIdx.x; idx < R * D; idx += blockDim.x) {
+        const int64_t r = idx / D;
+        float o = 0.0f;
+        for (int64_t c = 0; c < chunks; ++c) o = fmaf(po[c * R * D + idx], weights[c * R + r], o);
+        out[idx] = from_float<QT>(o);
     }
 }
 
@@ -324,6 +337,12 @@ sdc_status_t launch_simt_rows(const AttnArgs& a, int rpw, dim3 grid, size_t smem
 }
 
 template <typename QT>
+sdc_status_t launch_combine_typed(const AttnArgs& a, cudaStream_t st) {
+    attn_combine_kernel<QT><<<static_cast<unsigned>(a.batch * a.kv_heads), kCombineThreads, 0, st>>>(a);
+    return launch_status();
+}
+
+template <typename QT>
 sdc_status_t launch_simt_typed(const AttnArgs& a, cudaStream_t st) {
     const int rpw = static_cast<int>((a.rows + kWarps - 1) / kWarps);
     dim3 grid(static_cast<unsigned>(a.max_chunks), static_cast<unsigned>(a.batch * a.kv_heads));
@@ -337,17 +356,12 @@ sdc_status_t launch_simt_typed(const AttnArgs& a, cudaStream_t st) {
         default: return SDC_STATUS_UNSUPPORTED;
     }
     if (rc != SDC_STATUS_OK) return rc;
-    attn_combine_kernel<QT><<<static_cast<unsigned>(a.batch * a.kv_heads), 128, 0, st>>>(a);
-    return launch_status();
-}
-
-template <typename QT>
-sdc_status_t launch_combine_typed(const AttnArgs& a, cudaStream_t st) {
-    attn_combine_kernel<QT><<<static_cast<unsigned>(a.batch * a.kv_heads), 128, 0, st>>>(a);
-    return launch_status();
+    return launch_combine_typed<QT>(a, st);
 }
 
 }  // namespace
+
+bool combine_fits(int64_t max_chunks, int64_t rows) { return max_chunks * rows <= kCombineMaxWeights; }
 
 bool simt_supports(int64_t head_dim, int64_t rows) {
     return (head_dim == 16 || head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256) && rows >= 1 &&

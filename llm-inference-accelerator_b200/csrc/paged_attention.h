@@ -36,6 +36,8 @@ bool simt_supports(int64_t head_dim, int64_t rows);
 sdc_status_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream);
 // Merges the per-chunk partials into the output (used by both item kernels).
 sdc_status_t launch_attention_combine(const AttnArgs& a, cudaStream_t stream);
+// Whether max_chunks * rows chunk weights fit the combine's shared buffer.
+bool combine_fits(int64_t max_chunks, int64_t rows);
 
 namespace tc {
 // Shapes the tensor-core item kernel serves: head_dim 128 and at most 40

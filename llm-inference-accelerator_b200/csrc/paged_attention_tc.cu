@@ -6,27 +6,30 @@
 // items of (sequence, KV head, chunk), un-normalised partials, a combine
 // pass); what changes is how one item walks its chunk, 128 tokens per tile:
 //
-//   S^T[t, n] = sum_d K[t, d] * Qi8[n, d]      (M = 128 tokens, N = 2*RMAX cols)
+//   S^T[t, n] = sum_d K[t, d] * Qi8[n, d]      (M = 128 tokens, N columns)
 //   O^T[d, n] = sum_t V[t, d] * Pi8[n, t]      (M = 128 = head_dim, same N)
 //
-// The query rows are split into two INT8 parts, q ~ s1 * (hi + lo / 254)
-// with s1 = max|q| / 127 per row (columns [0, RMAX) hold hi, [RMAX, 2 RMAX)
-// lo), so the integer products are exact and the row's score is
-// (254 * S_hi + S_lo) * s1 / 254 * scale_k: the query carries 15 bits of
-// relative precision, finer than its bf16 input.  Probabilities are split
-// the same way after folding in the value scale: u = p * scale_v / max(scale_v)
-// in [0, 1], hi = rint(127 u), lo = rint(254 (127 u - hi)), an absolute error
-// below 1.6e-5.  K is the A operand in K-major form and V the A operand in
-// MN-major form of the same 128-byte rows: every page goes from HBM to
-// shared memory exactly once, by one TMA box per page, and is never
+// Query rows are split into two INT8 parts, q ~ s1 * (hi + lo / 254) with
+// s1 = max|q| / 127 per row (columns [0, RB) hold hi, [RB, 2 RB) lo, RB = the
+// row bucket), so the integer products are exact and a row's score is
+// (254 S_hi + S_lo) * s1 / 254 * scale_k: 15 bits of relative precision,
+// finer than the bf16 input.  Probabilities are split the same way after
+// folding in the value scale: x = 127 p scale_v / max(scale_v) in [0, 127],
+// hi = rint(x), lo = rint(254 (x - hi)), an absolute error below 1.6e-5 of
+// the tile's largest weight.  K is the A operand in K-major form and V the A
+// operand in MN-major form of the same 128-byte page rows: every page goes
+// from HBM to shared memory exactly once, one TMA box per page, and is never
 // converted.
 //
-// Warp roles (192 threads): warps 0-3 run softmax (thread = token of S^T,
-// TMEM lane) and the O epilogue (thread = head_dim row of O^T); warp 4
-// issues TMA; warp 5 allocates tensor memory and issues the MMAs.  Every
-// mbarrier wait gives up after one second, records SDC_FAULT_WAIT_TIMEOUT in
-// the status word, and lets the block wind down: it waits (bounded) for its
-// own copies and MMAs, frees tensor memory and returns.
+// Warp roles (320 threads, one block per SM): two softmax warpgroups take
+// alternate tiles (warpgroup k owns S/P/O buffer k; a thread is a token row of
+// S^T and a head_dim row of O^T, its TMEM lane), each with its own online
+// softmax state, merged at the end of an item; warp 8 quantizes the query
+// rows and issues TMA; warp 9 allocates tensor memory and issues the MMAs.
+// Every mbarrier wait gives up after one second, records
+// SDC_FAULT_WAIT_TIMEOUT in the status word, and lets the block wind down:
+// it waits (bounded) for its own copies and MMAs, frees tensor memory and
+// returns.  No named barriers: a warp that gives up can never strand another.
 
 #include <cuda.h>
 
@@ -42,49 +45,41 @@ namespace {
 
 constexpr int kTile = 128;     // tokens per tile (MMA M for S^T)
 constexpr int kHeadDim = 128;  // MMA M for O^T, and the K extent of S^T
-constexpr int kCodeTileBytes = kTile * kHeadDim;                    // 16 KiB
-constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;     // K, V codes + scales
-constexpr int kSoftmaxWarps = 4;
-constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kCodeTileBytes = kTile * kHeadDim;                 // 16 KiB
+constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;  // K, V codes + scales
+constexpr int kGroups = 2;                                       // softmax warpgroups
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = (kProducerWarp + 2) * 32;
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // one second
+constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
 
-constexpr int pow2_at_least(int v) {
-    int p = 32;
-    while (p < v) p <<= 1;
-    return p;
-}
-
-template <int RMAX, int STAGES>
-struct Layout {
-    static constexpr int N = ((2 * RMAX + 15) / 16) * 16;                  // MMA N
-    static constexpr int kQCodes = N * kHeadDim;                           // query image codes
-    static constexpr int kQBytes = kQCodes + ((RMAX * 4 + 15) / 16) * 16;   // + per-row factors
+template <int RB>
+struct Rows {
+    static constexpr int N = ((2 * RB + 15) / 16) * 16;  // MMA N
+    static constexpr int kStages = RB <= 24 ? 5 : 4;
+    static constexpr int kQCodes = N * kHeadDim;
     static constexpr int kPBytes = N * kTile;
-    static constexpr int kTmemStride = pow2_at_least(N);                   // columns per buffer
-    static constexpr int kTmemCols = 4 * kTmemStride;                      // S0 S1 O0 O1
-    // shared-memory offsets (bytes, from a 1024-aligned base)
-    static constexpr int kStages = 0;
-    static constexpr int kQ = kStages + STAGES * kStageBytes;
-    static constexpr int kP = kQ + 2 * ((kQBytes + 127) / 128) * 128;
-    static constexpr int kRed = kP + 2 * kPBytes;                 // [2][4][RMAX + 1] per-warp exchange
-    static constexpr int kAlpha = kRed + 2 * 4 * (RMAX + 1) * 4;  // [2][RMAX] rescale factors per tile parity
-    static constexpr int kVfac = kAlpha + 2 * RMAX * 4;           // [2]
-    static constexpr int kBar = ((kVfac + 8 + 7) / 8) * 8;        // mbarriers
-    static constexpr int kNumBars = 2 * STAGES + 2 * 8;
-    static constexpr int kMisc = kBar + kNumBars * 8;             // tmem base, abort flag
-    static constexpr int kTotal = kMisc + 16;
-    static constexpr int kDynamicSmem = kTotal + 1024;            // room to align the base
+    static constexpr int kTmemStride = N <= 64 ? 64 : 128;  // columns per S / O buffer
+    static constexpr int kTmemCols = 4 * kTmemStride;       // S0 S1 O0 O1
+    // shared-memory offsets from a 1024-aligned base
+    static constexpr int kStageOff = 0;
+    static constexpr int kQOff = kStages * kStageBytes;                           // 2 query images
+    static constexpr int kQFacOff = kQOff + 2 * kQCodes;                          // [2][RB] row factors
+    static constexpr int kPOff = ((kQFacOff + 2 * RB * 4 + 1023) / 1024) * 1024;  // 2 P tiles
+    static constexpr int kRedOff = kPOff + 2 * kPBytes;  // [group][parity][warp][RB + 1]
+    static constexpr int kAlphaOff = kRedOff + kGroups * 2 * 4 * (RB + 1) * 4;  // [group][parity][RB]
+    static constexpr int kChgOff = kAlphaOff + kGroups * 2 * RB * 4;            // [group][parity] u32
+    static constexpr int kVfacOff = kChgOff + kGroups * 2 * 4;                  // [group][parity]
+    static constexpr int kMergeOOff = kVfacOff + kGroups * 2 * 4;               // [128][RB]
+    static constexpr int kMergeMLOff = kMergeOOff + 128 * RB * 4;               // [RB][2]
+    static constexpr int kBarOff = ((kMergeMLOff + RB * 8 + 7) / 8) * 8;
+    static constexpr int kNumBars = 2 * kStages + 2 * 7 + 2 * kGroups + 2;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+    static constexpr int kTotal = kMiscOff + 16;
+    static constexpr int kDynamicSmem = kTotal + 1024;
+    static_assert(RB <= 32, "row masks are 32 bits");
 };
-
-// Pipeline depth and blocks per SM by row bucket: 24 rows fit two blocks per
-// SM (256 TMEM columns and ~93 KB of shared memory each); 40 rows take the
-// whole tensor memory (512 columns), so one block with a deeper pipeline.
-template <int RMAX>
-constexpr int kStagesFor = RMAX <= 24 ? 2 : 3;
-template <int RMAX>
-constexpr int kMinBlocksFor = RMAX <= 24 ? 2 : 1;
 
 struct WorkItem {
     int32_t b, h, t0, t1;
@@ -92,11 +87,9 @@ struct WorkItem {
 
 struct TcArgs {
     AttnArgs a;
-    const uint8_t* qimg;    // [B * Hkv][q_bytes]
-    int32_t q_bytes;
-    const WorkItem* items;  // [max_items]
+    const WorkItem* items;
     const int32_t* item_count;
-    int32_t rows;           // query rows per KV head (<= RMAX)
+    int32_t rows;  // query rows per KV head (<= RB)
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -219,14 +212,12 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 }
 
 // 16 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16], int base) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
-        : "=r"(r[base + 0]), "=r"(r[base + 1]), "=r"(r[base + 2]), "=r"(r[base + 3]), "=r"(r[base + 4]),
-          "=r"(r[base + 5]), "=r"(r[base + 6]), "=r"(r[base + 7]), "=r"(r[base + 8]), "=r"(r[base + 9]),
-          "=r"(r[base + 10]), "=r"(r[base + 11]), "=r"(r[base + 12]), "=r"(r[base + 13]), "=r"(r[base + 14]),
-          "=r"(r[base + 15])
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
 
@@ -234,12 +225,7 @@ template <int N>
 __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, uint32_t (&r)[N]) {
     static_assert(N % 16 == 0, "columns come in groups of 16");
 #pragma unroll
-    for (int c = 0; c < N; c += 16) {
-        uint32_t chunk[16];
-        tmem_ld16(taddr + c, chunk, 0);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) r[c + i] = chunk[i];
-    }
+    for (int c = 0; c < N; c += 16) tmem_ld16(taddr + c, r + c);
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
@@ -255,17 +241,28 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-__device__ __forceinline__ uint32_t byte_of(int v, int i) { return (static_cast<uint32_t>(v) & 0xffu) << (8 * i); }
+__device__ __forceinline__ float fast_exp2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Low bytes of four words packed into one word (byte i from w_i).
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+    return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
+}
 
 // ---------------------------------------------------------------- main kernel
 
-template <int RMAX, int STAGES, int MIN_BLOCKS>
-__global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
+template <int RB>
+__global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, TcArgs t) {
-    using LY = Layout<RMAX, STAGES>;
+    using LY = Rows<RB>;
     constexpr int N = LY::N;
+    constexpr int STAGES = LY::kStages;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const AttnArgs& a = t.a;
 
     const int warp = threadIdx.x >> 5;
@@ -273,31 +270,37 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
     const int count = __ldg(t.item_count);
     if (static_cast<int>(blockIdx.x) >= count) return;  // whole block: no work
 
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kBar);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kBarOff);
     auto bar = [&](int i) { return smem_u32(bars + i); };
-    // barrier indices
     const int kvFull = 0, kvEmpty = STAGES, qFull = 2 * STAGES, qEmpty = qFull + 2, sFull = qEmpty + 2,
-              sEmpty = sFull + 2, pFull = sEmpty + 2, oFull = pFull + 2, oEmpty = oFull + 2, xch = oEmpty + 2;
-    volatile uint32_t* tmem_base_slot = reinterpret_cast<volatile uint32_t*>(smem + LY::kMisc);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::kMisc + 4);
+              sEmpty = sFull + 2, pFull = sEmpty + 2, oFull = pFull + 2, oEmpty = oFull + 2,
+              xch = oEmpty + 2 /* [group][parity] */, mergeFull = xch + 2 * kGroups, mergeEmpty = mergeFull + 1;
+    volatile uint32_t* tmem_base_slot = reinterpret_cast<volatile uint32_t*>(smem + LY::kMiscOff);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::kMiscOff + 4);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(bar(kvFull + s), 1);
-            mbar_init(bar(kvEmpty + s), 1 + kSoftmaxWarps);
+            mbar_init(bar(kvEmpty + s), 1 + 4);  // MMA commit + the consuming warpgroup
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(qFull + i), 1);
-            mbar_init(bar(qEmpty + i), 1 + kSoftmaxWarps);
+            mbar_init(bar(qEmpty + i), 1 + 4 * kGroups);
             mbar_init(bar(sFull + i), 1);
-            mbar_init(bar(sEmpty + i), kSoftmaxWarps);
-            mbar_init(bar(pFull + i), kSoftmaxWarps * 32);
+            mbar_init(bar(sEmpty + i), 4);
+            mbar_init(bar(pFull + i), 128);
             mbar_init(bar(oFull + i), 1);
-            mbar_init(bar(oEmpty + i), kSoftmaxWarps);
-            mbar_init(bar(xch + i), kSoftmaxWarps);
+            mbar_init(bar(oEmpty + i), 4);
         }
+        for (int i = 0; i < 2 * kGroups; ++i) mbar_init(bar(xch + i), 4);
+        mbar_init(bar(mergeFull), 4);
+        mbar_init(bar(mergeEmpty), 4);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // query images: rows past `rows` stay zero for the whole kernel
+    for (int i = threadIdx.x; i < 2 * LY::kQCodes / 16; i += blockDim.x) {
+        reinterpret_cast<uint4*>(smem + LY::kQOff)[i] = make_uint4(0u, 0u, 0u, 0u);
     }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -311,26 +314,78 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
     tc_fence_after();
     const uint32_t tmem = *tmem_base_slot;
 
-    const uint32_t stage_base = smem_u32(smem + LY::kStages);
-    const uint32_t q_base = smem_u32(smem + LY::kQ);
-    constexpr uint32_t kQStride = ((LY::kQBytes + 127) / 128) * 128;
-    const uint32_t p_base = smem_u32(smem + LY::kP);
+    const uint32_t stage_base = smem_u32(smem + LY::kStageOff);
+    const uint32_t q_base = smem_u32(smem + LY::kQOff);
+    const uint32_t p_base = smem_u32(smem + LY::kPOff);
     const int R = t.rows;
     const int64_t bs = a.pool.block_size;
     const int pages_per_tile = static_cast<int>(kTile / bs);
 
     if (warp == kProducerWarp) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ query rows + TMA
         uint32_t g = 0, li = 0;
         for (int item = blockIdx.x; item < count; item += gridDim.x, ++li) {
             const WorkItem it = t.items[item];
             const uint32_t qb = li & 1;
             if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status)) break;
-            if (lane == 0) {
-                mbar_arrive_expect_tx(bar(qFull + qb), t.q_bytes);
-                bulk_load(q_base + qb * kQStride,
-                          t.qimg + (static_cast<int64_t>(it.b) * a.kv_heads + it.h) * t.q_bytes, t.q_bytes,
-                          bar(qFull + qb));
+            {
+                // Split each query row into INT8 hi / lo parts, laid out as the
+                // B operand of the score MMA (K-major, no swizzle: 8 rows x 16
+                // bytes per 128-byte core matrix, 16-byte K chunks 128 bytes
+                // apart, 8-row groups 1024 bytes apart).
+                const int64_t qrow0 = (static_cast<int64_t>(it.b) * a.query_heads + it.h * a.group) * a.window;
+                unsigned char* img = smem + LY::kQOff + qb * LY::kQCodes;
+                float* fac = reinterpret_cast<float*>(smem + LY::kQFacOff) + qb * RB;
+                const int d = lane * 4;
+                for (int r = 0; r < R; ++r) {
+                    float x[4];
+                    const int64_t e = (qrow0 + r) * kHeadDim + d;
+                    if (a.query_dtype == SDC_DTYPE_BF16) {
+                        const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.query) + e);
+                        x[0] = __uint_as_float(w.x << 16);
+                        x[1] = __uint_as_float(w.x & 0xffff0000u);
+                        x[2] = __uint_as_float(w.y << 16);
+                        x[3] = __uint_as_float(w.y & 0xffff0000u);
+                    } else if (a.query_dtype == SDC_DTYPE_F16) {
+                        const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const __half*>(a.query) + e);
+                        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+                        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+                        x[0] = lo.x;
+                        x[1] = lo.y;
+                        x[2] = hi.x;
+                        x[3] = hi.y;
+                    } else {
+                        const float4 w = *reinterpret_cast<const float4*>(static_cast<const float*>(a.query) + e);
+                        x[0] = w.x;
+                        x[1] = w.y;
+                        x[2] = w.z;
+                        x[3] = w.w;
+                    }
+                    float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
+                    uint32_t hi_word = 0, lo_word = 0;
+                    float factor = 0.0f;
+                    if (m > 0.0f) {
+                        const float s1 = m / 127.0f;
+                        const float inv = 1.0f / s1;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float hi = fminf(fmaxf(rintf(x[i] * inv), -127.0f), 127.0f);
+                            const float lo = fminf(fmaxf(rintf((x[i] - hi * s1) * (254.0f * inv)), -127.0f), 127.0f);
+                            hi_word |= (static_cast<uint32_t>(static_cast<int>(hi)) & 0xffu) << (8 * i);
+                            lo_word |= (static_cast<uint32_t>(static_cast<int>(lo)) & 0xffu) << (8 * i);
+                        }
+                        factor = s1 / 254.0f * a.qk_scale;
+                    }
+                    auto offset = [&](int n) { return (n >> 3) * 1024 + (d >> 4) * 128 + (n & 7) * 16 + (d & 15); };
+                    *reinterpret_cast<uint32_t*>(img + offset(r)) = hi_word;
+                    *reinterpret_cast<uint32_t*>(img + offset(RB + r)) = lo_word;
+                    if (lane == 0) fac[r] = factor;
+                }
+                fence_proxy_async();  // the tensor core reads the image through the async proxy
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(qFull + qb));
             }
             const int32_t* table = a.block_tables + static_cast<int64_t>(it.b) * a.table_stride;
             const int64_t code_base = a.layer * a.pool.cls + it.h * a.pool.chs;
@@ -358,8 +413,7 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
                 __syncwarp();
                 if (valid) {
                     const uint32_t st = stage_base + s * kStageBytes;
-                    const int64_t code_off = blk * a.pool.cbs + code_base;
-                    const int32_t row = static_cast<int32_t>(code_off / kHeadDim);
+                    const int32_t row = static_cast<int32_t>((blk * a.pool.cbs + code_base) / kHeadDim);
                     const uint32_t dst = static_cast<uint32_t>(lane * bs * kHeadDim);
                     tma_load_2d(st + dst, &kmap, 0, row, bar(kvFull + s));
                     tma_load_2d(st + kCodeTileBytes + dst, &vmap, 0, row, bar(kvFull + s));
@@ -373,8 +427,7 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
             }
             if (stop) break;
         }
-        // wind down: every copy this warp issued has landed before the block exits
-        if (*abort_flag && lane == 0) {
+        if (*abort_flag && lane == 0) {  // every copy issued has landed before the block exits
             for (uint32_t k = 0; k < STAGES && k < g; ++k) {
                 const uint32_t gg = g - 1 - k;
                 drain_phase(bar(kvFull + gg % STAGES), (gg / STAGES) & 1);
@@ -385,10 +438,8 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
         constexpr uint32_t kIdescS = idesc_i8(kTile, N, 0, 0);
         constexpr uint32_t kIdescO = idesc_i8(kHeadDim, N, 1, 1);
         uint32_t g = 0, li = 0;
-        bool have_prev = false;
-        uint32_t prev = 0;
-        uint32_t last_s_commit = 0, last_o_commit = 0;
-        bool any_s = false, any_o = false;
+        bool have_prev = false, any_s = false, any_o = false;
+        uint32_t prev = 0, last_s = 0, last_o = 0;
         auto issue_pv = [&](uint32_t gp) -> bool {
             const uint32_t sb = gp & 1;
             const uint32_t s = gp % STAGES;
@@ -408,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
                 mma_commit(bar(kvEmpty + s));
             }
             __syncwarp();
-            last_o_commit = gp;
+            last_o = gp;
             any_o = true;
             return true;
         };
@@ -428,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t k_tile = stage_base + s * kStageBytes;
-                    const uint32_t q_tile = q_base + qb * kQStride;
+                    const uint32_t q_tile = q_base + qb * LY::kQCodes;
 #pragma unroll
                     for (int ks = 0; ks < kHeadDim / 32; ++ks) {
                         const uint64_t da = smem_desc(k_tile + ks * 32, 16, 1024, 2);
@@ -439,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
                     if (tile0 + kTile >= it.t1) mma_commit(bar(qEmpty + qb));
                 }
                 __syncwarp();
-                last_s_commit = g;
+                last_s = g;
                 any_s = true;
                 if (have_prev && !issue_pv(prev)) {
                     ok = false;
@@ -452,190 +503,252 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
         }
         if (ok && have_prev) issue_pv(prev);
         if (*abort_flag && lane == 0) {
-            if (any_s) drain_phase(bar(sFull + (last_s_commit & 1)), (last_s_commit >> 1) & 1);
-            if (any_o) drain_phase(bar(oFull + (last_o_commit & 1)), (last_o_commit >> 1) & 1);
+            if (any_s) drain_phase(bar(sFull + (last_s & 1)), (last_s >> 1) & 1);
+            if (any_o) drain_phase(bar(oFull + (last_o & 1)), (last_o >> 1) & 1);
         }
     } else {
         // ------------------------------------------------------------ softmax + O epilogue
-        // Cross-warp exchanges go through shared memory guarded by the xch
-        // mbarriers (one arrival per warp), double-buffered by exchange
-        // parity: a buffer is rewritten two exchanges later, by which time
-        // every warp has arrived at the exchange in between and so has
-        // finished reading it.
-        float* red = reinterpret_cast<float*>(smem + LY::kRed);      // [2][4][RMAX + 1]
-        float* alpha_s = reinterpret_cast<float*>(smem + LY::kAlpha);
-        float* vfac_s = reinterpret_cast<float*>(smem + LY::kVfac);
-        constexpr int kRedStride = RMAX + 1;
-        const int tid = threadIdx.x;  // 0..127: token row of S^T, head_dim row of O^T
-        const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
-        uint32_t g = 0, li = 0, xc = 0;
-        // publish this warp's slice of red[xc], wait for all four warps
+        // Warpgroup `grp` takes the tiles with g % 2 == grp.  Cross-warp data
+        // goes through shared memory guarded by the group's xch mbarriers
+        // (one arrival per warp), double-buffered by exchange parity: a buffer
+        // is rewritten two exchanges later, by which time every warp of the
+        // group has arrived at the exchange in between and so has finished
+        // reading it.  Per-tile rescale data (alpha, changed-row mask, value
+        // factor) are double-buffered by the group's tile parity.
+        const int grp = warp >> 2;
+        const int qw = warp & 3;            // lane quarter = TMEM lanes [32 qw, 32 qw + 32)
+        const int tid = threadIdx.x & 127;  // token row of S^T, head_dim row of O^T
+        const uint32_t lane_addr = static_cast<uint32_t>(qw * 32) << 16;
+        const uint32_t s_col = grp * LY::kTmemStride;
+        const uint32_t o_col = (2 + grp) * LY::kTmemStride;
+        float* red = reinterpret_cast<float*>(smem + LY::kRedOff) + grp * 2 * 4 * (RB + 1);
+        float* alpha_s = reinterpret_cast<float*>(smem + LY::kAlphaOff) + grp * 2 * RB;
+        uint32_t* chg_s = reinterpret_cast<uint32_t*>(smem + LY::kChgOff) + grp * 2;
+        float* vfac_s = reinterpret_cast<float*>(smem + LY::kVfacOff) + grp * 2;
+        float* merge_o = reinterpret_cast<float*>(smem + LY::kMergeOOff);
+        float* merge_ml = reinterpret_cast<float*>(smem + LY::kMergeMLOff);
+        uint32_t g = 0, li = 0, xc = 0, own = 0, merges = 0;
+
         auto exchange = [&]() -> bool {
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(xch + (xc & 1)));
-            const bool ok = warp_wait(bar(xch + (xc & 1)), (xc >> 1) & 1, abort_flag, a.status);
-            return ok;
+            if (lane == 0) mbar_arrive(bar(xch + grp * 2 + (xc & 1)));
+            return warp_wait(bar(xch + grp * 2 + (xc & 1)), (xc >> 1) & 1, abort_flag, a.status);
         };
-        auto epilogue = [&](uint32_t gp, float (&o_acc)[RMAX]) -> bool {
-            const uint32_t ob = gp & 1;
-            if (!warp_wait(bar(oFull + ob), (gp >> 1) & 1, abort_flag, a.status)) return false;
+        // O^T tile of this group's k-th tile (the MMA warp alternates buffers
+        // by tile, so the group's k-th use of its O buffer has parity k & 1)
+        auto epilogue = [&](uint32_t k, float (&o_acc)[RB]) -> bool {
+            if (!warp_wait(bar(oFull + grp), k & 1, abort_flag, a.status)) return false;
             tc_fence_after();
             uint32_t oreg[N];
-            tmem_ld_row<N>(tmem + lane_addr + (2 + ob) * LY::kTmemStride, oreg);
+            tmem_ld_row<N>(tmem + lane_addr + o_col, oreg);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(oEmpty + ob));
-            const float vf = vfac_s[ob];
+            if (lane == 0) mbar_arrive(bar(oEmpty + grp));
+            const int par = k & 1;
+            const float vf = vfac_s[par];
+            const uint32_t chg = chg_s[par];
 #pragma unroll
-            for (int r = 0; r < RMAX; ++r) {
-                const int32_t combined = static_cast<int32_t>(oreg[r]) * 254 + static_cast<int32_t>(oreg[RMAX + r]);
-                o_acc[r] = o_acc[r] * alpha_s[ob * RMAX + r] + static_cast<float>(combined) * vf;
+            for (int r = 0; r < RB; ++r) {
+                const int32_t combined = static_cast<int32_t>(oreg[r]) * 254 + static_cast<int32_t>(oreg[RB + r]);
+                const float prev = ((chg >> r) & 1) ? o_acc[r] * alpha_s[par * RB + r] : o_acc[r];
+                o_acc[r] = fmaf(static_cast<float>(combined), vf, prev);
             }
             return true;
         };
+
         bool ok = true;
         for (int item = blockIdx.x; item < count && ok; item += gridDim.x, ++li) {
             const WorkItem it = t.items[item];
             const uint32_t qb = li & 1;
             if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status)) break;
-            const float* qfac = reinterpret_cast<const float*>(smem + LY::kQ + qb * kQStride + LY::kQCodes);
+            const float* qfac = reinterpret_cast<const float*>(smem + LY::kQFacOff) + qb * RB;
             const int64_t T = __ldg(a.context_lens + it.b);
             const int64_t window = a.window;
-            float m_run[RMAX], l_thr[RMAX], o_acc[RMAX];
+            float m_lane = -INFINITY;  // lane r holds the running max of row r
+            float l_thr[RB], o_acc[RB];
 #pragma unroll
-            for (int r = 0; r < RMAX; ++r) {
-                m_run[r] = -INFINITY;
+            for (int r = 0; r < RB; ++r) {
                 l_thr[r] = 0.0f;
                 o_acc[r] = 0.0f;
             }
-            const uint32_t first_g = g;
+            bool have_prev = false;
+            uint32_t prev_own = 0;
             for (int tile0 = it.t0; tile0 < it.t1; tile0 += kTile, ++g) {
-                const uint32_t sb = g & 1;
+                if (static_cast<int>(g & 1) != grp) continue;
                 const uint32_t s = g % STAGES;
-                if (!warp_wait(bar(sFull + sb), (g >> 1) & 1, abort_flag, a.status) ||
+                if (!warp_wait(bar(sFull + grp), own & 1, abort_flag, a.status) ||
                     !warp_wait(bar(kvFull + s), (g / STAGES) & 1, abort_flag, a.status)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 uint32_t sreg[N];
-                tmem_ld_row<N>(tmem + lane_addr + sb * LY::kTmemStride, sreg);
+                tmem_ld_row<N>(tmem + lane_addr + s_col, sreg);
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(sEmpty + sb));
+                if (lane == 0) mbar_arrive(bar(sEmpty + grp));
 
                 const int64_t tok = tile0 + tid;
                 const bool tvalid = tok < it.t1;
-                const float* stage_scales =
-                    reinterpret_cast<const float*>(smem + LY::kStages + s * kStageBytes + 2 * kCodeTileBytes);
-                const float kscale = stage_scales[tid];
-                const float vscale = tvalid ? stage_scales[kTile + tid] : 0.0f;
+                const float* sc_ptr =
+                    reinterpret_cast<const float*>(smem + LY::kStageOff + s * kStageBytes + 2 * kCodeTileBytes);
+                const float kscale = sc_ptr[tid];
+                const float vscale = tvalid ? sc_ptr[kTile + tid] : 0.0f;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kvEmpty + s));
 
                 // a query at window row i sees keys up to T - window + i; only
                 // tiles reaching into the window need the per-row test
                 const bool causal_tile = tile0 + kTile > T - window;
-                auto visible = [&](int r) {
-                    if (!tvalid || r >= R) return false;
-                    return !causal_tile || tok <= T - window + (r % window);
-                };
-                float* red_x = red + (xc & 1) * 4 * kRedStride;
+                float sc[RB];
+                float* red_x = red + (xc & 1) * 4 * (RB + 1);
 #pragma unroll
-                for (int r = 0; r < RMAX; ++r) {
-                    float sc = -INFINITY;
-                    if (visible(r)) {
-                        const int32_t combined =
-                            static_cast<int32_t>(sreg[r]) * 254 + static_cast<int32_t>(sreg[RMAX + r]);
-                        sc = static_cast<float>(combined) * (qfac[r] * kscale);
-                    }
-                    const float wm = redux_max(sc);
-                    if (lane == 0) red_x[warp * kRedStride + r] = wm;
+                for (int r = 0; r < RB; ++r) {
+                    bool vis = tvalid && r < R;
+                    if (causal_tile) vis = vis && tok <= T - window + (r % window);
+                    const int32_t combined = static_cast<int32_t>(sreg[r]) * 254 + static_cast<int32_t>(sreg[RB + r]);
+                    sc[r] = vis ? static_cast<float>(combined) * (qfac[r] * kscale) : -INFINITY;
+                    const float wm = redux_max(sc[r]);
+                    if (lane == 0) red_x[qw * (RB + 1) + r] = wm;
                 }
-                const float wv = redux_max(vscale);
-                if (lane == 0) red_x[warp * kRedStride + RMAX] = wv;
+                {
+                    const float wv = redux_max(vscale);
+                    if (lane == 0) red_x[qw * (RB + 1) + RB] = wv;
+                }
                 if (!exchange()) {
                     ok = false;
                     break;
                 }
                 ++xc;
-                const float vmax = fmaxf(fmaxf(red_x[RMAX], red_x[kRedStride + RMAX]),
-                                         fmaxf(red_x[2 * kRedStride + RMAX], red_x[3 * kRedStride + RMAX]));
-                const float u_scale = vmax > 0.0f ? 127.0f * vscale / vmax : 0.0f;
-                uint32_t row_words[N / 4];
-#pragma unroll
-                for (int w = 0; w < N / 4; ++w) row_words[w] = 0u;
-#pragma unroll
-                for (int r = 0; r < RMAX; ++r) {
-                    const float tmax = fmaxf(fmaxf(red_x[r], red_x[kRedStride + r]),
-                                             fmaxf(red_x[2 * kRedStride + r], red_x[3 * kRedStride + r]));
-                    const float m_new = fmaxf(m_run[r], tmax);
-                    const float alpha = (m_new == -INFINITY) ? 1.0f : exp2f(m_run[r] - m_new);
-                    m_run[r] = m_new;
-                    float p = 0.0f;
-                    if (visible(r)) {
-                        const int32_t combined =
-                            static_cast<int32_t>(sreg[r]) * 254 + static_cast<int32_t>(sreg[RMAX + r]);
-                        p = exp2f(static_cast<float>(combined) * (qfac[r] * kscale) - m_new);
-                    }
-                    l_thr[r] = l_thr[r] * alpha + p;
-                    const float x = p * u_scale;  // in [0, 127]
-                    const float hi = rintf(x);
-                    const float lo = rintf((x - hi) * 254.0f);
-                    row_words[r / 4] |= byte_of(static_cast<int>(hi), r % 4);
-                    row_words[(RMAX + r) / 4] |= byte_of(static_cast<int>(lo), (RMAX + r) % 4);
-                    if (tid == r) alpha_s[sb * RMAX + r] = alpha;
+                // lane r resolves row r: tile max over the four warps, new
+                // running max, and the rescale factor when the max moved
+                float m_new_lane = -INFINITY, alpha_lane = 1.0f;
+                if (lane < RB) {
+                    const float tmax = fmaxf(fmaxf(red_x[lane], red_x[(RB + 1) + lane]),
+                                             fmaxf(red_x[2 * (RB + 1) + lane], red_x[3 * (RB + 1) + lane]));
+                    m_new_lane = fmaxf(m_lane, tmax);
+                    if (m_new_lane > m_lane) alpha_lane = (m_lane == -INFINITY) ? 0.0f : fast_exp2(m_lane - m_new_lane);
                 }
-                if (tid == 0) vfac_s[sb] = vmax / (127.0f * 254.0f);
-                // P^T row of this token (columns [0, RMAX) hi, [RMAX, 2 RMAX) lo,
-                // rest zero) in the MN-major no-swizzle layout: a 128-byte core
-                // matrix holds 16 columns x 8 tokens; 8-token groups are 128 bytes
-                // apart, 16-column groups 2048 bytes apart.
-                unsigned char* prow = smem + LY::kP + sb * LY::kPBytes + (tid >> 3) * 128 + (tid & 7) * 16;
+                const uint32_t changed = __ballot_sync(kFullMask, lane < RB && m_new_lane > m_lane);
+                m_lane = m_new_lane;
+                const float vmax = fmaxf(fmaxf(red_x[RB], red_x[(RB + 1) + RB]),
+                                         fmaxf(red_x[2 * (RB + 1) + RB], red_x[3 * (RB + 1) + RB]));
+                const float u_scale = vmax > 0.0f ? 127.0f * vscale / vmax : 0.0f;
+                static_assert(RB % 4 == 0, "rows are packed four to a word");
+                uint32_t words[N / 4];  // P^T row: hi bytes in columns [0, RB), lo in [RB, 2 RB)
+#pragma unroll
+                for (int w = 0; w < N / 4; ++w) words[w] = 0u;
+#pragma unroll
+                for (int r4 = 0; r4 < RB; r4 += 4) {
+                    uint32_t th_bits[4], tl_bits[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int r = r4 + j;
+                        const float m_r = __shfl_sync(kFullMask, m_new_lane, r);
+                        const float alpha_r = __shfl_sync(kFullMask, alpha_lane, r);
+                        if ((changed >> r) & 1) l_thr[r] *= alpha_r;
+                        const float p = sc[r] == -INFINITY ? 0.0f : fast_exp2(sc[r] - m_r);
+                        l_thr[r] += p;
+                        // x in [0, 127]: hi = rint(x), lo = rint(254 (x - hi)); adding
+                        // 1.5 * 2^23 leaves the rounded integer in the low mantissa bits
+                        const float x = p * u_scale;
+                        const float th = x + kRoundMagic;
+                        const float hi = th - kRoundMagic;
+                        const float tl = fmaf(x - hi, 254.0f, kRoundMagic);
+                        th_bits[j] = __float_as_uint(th);
+                        tl_bits[j] = __float_as_uint(tl);
+                        if (tid == r) alpha_s[(own & 1) * RB + r] = alpha_r;
+                    }
+                    words[r4 / 4] = pack_low_bytes(th_bits[0], th_bits[1], th_bits[2], th_bits[3]);
+                    words[(RB + r4) / 4] = pack_low_bytes(tl_bits[0], tl_bits[1], tl_bits[2], tl_bits[3]);
+                }
+                if (tid == 0) {
+                    chg_s[own & 1] = changed;
+                    vfac_s[own & 1] = vmax / (127.0f * 254.0f);
+                }
+                // P^T row of this token in the MN-major no-swizzle layout: a
+                // 128-byte core matrix holds 16 columns x 8 tokens; 8-token
+                // groups are 128 bytes apart, 16-column groups 2048 apart.
+                unsigned char* prow = smem + LY::kPOff + grp * LY::kPBytes + (tid >> 3) * 128 + (tid & 7) * 16;
 #pragma unroll
                 for (int c = 0; c < N / 16; ++c) {
                     *reinterpret_cast<uint4*>(prow + c * 2048) =
-                        make_uint4(row_words[4 * c], row_words[4 * c + 1], row_words[4 * c + 2], row_words[4 * c + 3]);
+                        make_uint4(words[4 * c], words[4 * c + 1], words[4 * c + 2], words[4 * c + 3]);
                 }
                 fence_proxy_async();
-                mbar_arrive(bar(pFull + sb));
+                mbar_arrive(bar(pFull + grp));
 
-                if (g > first_g && !epilogue(g - 1, o_acc)) {  // previous tile of this item
+                if (have_prev && !epilogue(prev_own, o_acc)) {
                     ok = false;
                     break;
                 }
+                have_prev = true;
+                prev_own = own;
+                ++own;
             }
             if (!ok) break;
-            // publish the last tile's alpha / vfac, then its epilogue
+            // publish the last tile's rescale data, then its epilogue
             if (!exchange()) break;
             ++xc;
-            if (!epilogue(g - 1, o_acc)) break;
+            if (have_prev && !epilogue(prev_own, o_acc)) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(qEmpty + qb));
-            // partial result of this chunk: m, l (summed over all 128 tokens) and O
-            float* red_x = red + (xc & 1) * 4 * kRedStride;
+            // this group's row sums over all its tokens
+            float* red_x = red + (xc & 1) * 4 * (RB + 1);
 #pragma unroll
-            for (int r = 0; r < RMAX; ++r) {
+            for (int r = 0; r < RB; ++r) {
                 const float ws = warp_sum(l_thr[r]);
-                if (lane == 0) red_x[warp * kRedStride + r] = ws;
+                if (lane == 0) red_x[qw * (RB + 1) + r] = ws;
             }
             if (!exchange()) break;
             ++xc;
-            const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
-            const int64_t chunk = it.t0 / a.chunk;
-            float* part_o = a.part_o + (bh * a.max_chunks + chunk) * R * kHeadDim;
-            float* part_ml = a.part_ml + (bh * a.max_chunks + chunk) * R * 2;
-#pragma unroll
-            for (int r = 0; r < RMAX; ++r) {
-                if (r < R) {
-                    part_o[r * kHeadDim + tid] = o_acc[r];
-                    if (tid == r) {
-                        part_ml[2 * r + 0] = m_run[r];
-                        part_ml[2 * r + 1] = red_x[r] + red_x[kRedStride + r] + red_x[2 * kRedStride + r] +
-                                             red_x[3 * kRedStride + r];
-                    }
-                }
+            float l_lane = 0.0f;
+            if (lane < RB) {
+                l_lane = red_x[lane] + red_x[(RB + 1) + lane] + red_x[2 * (RB + 1) + lane] +
+                         red_x[3 * (RB + 1) + lane];
             }
+            // merge the two groups' states: group 1 hands its state to group 0
+            if (grp == 1) {
+                if (!warp_wait(bar(mergeEmpty), (merges & 1) ^ 1, abort_flag, a.status)) break;
+#pragma unroll
+                for (int r = 0; r < RB; ++r) merge_o[tid * RB + r] = o_acc[r];
+                if (qw == 0 && lane < RB) {
+                    merge_ml[2 * lane + 0] = m_lane;
+                    merge_ml[2 * lane + 1] = l_lane;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(mergeFull));
+            } else {
+                if (!warp_wait(bar(mergeFull), merges & 1, abort_flag, a.status)) break;
+                float e0_lane = 0.0f, e1_lane = 0.0f, m_tot = -INFINITY, l_tot = 0.0f;
+                if (lane < RB) {
+                    const float m1 = merge_ml[2 * lane + 0];
+                    const float l1 = merge_ml[2 * lane + 1];
+                    m_tot = fmaxf(m_lane, m1);
+                    if (m_tot != -INFINITY) {
+                        e0_lane = m_lane == -INFINITY ? 0.0f : fast_exp2(m_lane - m_tot);
+                        e1_lane = m1 == -INFINITY ? 0.0f : fast_exp2(m1 - m_tot);
+                    }
+                    l_tot = l_lane * e0_lane + l1 * e1_lane;
+                }
+                const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
+                const int64_t chunk = it.t0 / a.chunk;
+                float* part_o = a.part_o + (bh * a.max_chunks + chunk) * R * kHeadDim;
+                float* part_ml = a.part_ml + (bh * a.max_chunks + chunk) * R * 2;
+#pragma unroll
+                for (int r = 0; r < RB; ++r) {
+                    const float e0 = __shfl_sync(kFullMask, e0_lane, r);
+                    const float e1 = __shfl_sync(kFullMask, e1_lane, r);
+                    if (r < R) part_o[r * kHeadDim + tid] = o_acc[r] * e0 + merge_o[tid * RB + r] * e1;
+                }
+                if (qw == 0 && lane < R) {
+                    part_ml[2 * lane + 0] = m_tot;
+                    part_ml[2 * lane + 1] = l_tot;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(mergeEmpty));
+            }
+            ++merges;
         }
     }
 
@@ -646,56 +759,6 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS)
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(LY::kTmemCols)
                      : "memory");
-    }
-}
-
-// ---------------------------------------------------------------- query images
-
-// Splits each query row into INT8 hi/lo parts laid out as the B operand of
-// the score MMA (K-major, no swizzle: 8 rows x 16 bytes per 128-byte core
-// matrix, 16-byte K chunks 128 bytes apart, 8-row groups 1024 bytes apart),
-// followed by the per-row factor s1 / 254 * log2(e) / sqrt(D).
-template <typename QT, int RMAX>
-__global__ void __launch_bounds__(256) query_image_kernel(TcArgs t) {
-    using LY = Layout<RMAX, kStagesFor<RMAX>>;
-    const AttnArgs& a = t.a;
-    const int64_t bh = blockIdx.x;
-    const int64_t b = bh / a.kv_heads;
-    const int64_t h = bh - b * a.kv_heads;
-    uint8_t* img = const_cast<uint8_t*>(t.qimg) + bh * t.q_bytes;
-    for (int i = threadIdx.x; i < t.q_bytes / 16; i += blockDim.x) {
-        reinterpret_cast<uint4*>(img)[i] = make_uint4(0u, 0u, 0u, 0u);
-    }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const QT* q = static_cast<const QT*>(a.query) + ((b * a.query_heads + h * a.group) * a.window) * kHeadDim;
-    float* factors = reinterpret_cast<float*>(img + LY::kQCodes);
-    for (int r = warp; r < t.rows; r += blockDim.x / 32) {
-        float x[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) x[i] = static_cast<float>(q[r * kHeadDim + lane * 4 + i]);
-        float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
-        uint32_t hi_word = 0, lo_word = 0;
-        float factor = 0.0f;
-        if (m > 0.0f) {
-            const float s1 = m / 127.0f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float hi = fminf(fmaxf(rintf(x[i] / s1), -127.0f), 127.0f);
-                const float lo = fminf(fmaxf(rintf((x[i] - hi * s1) * (254.0f / s1)), -127.0f), 127.0f);
-                hi_word |= byte_of(static_cast<int>(hi), i);
-                lo_word |= byte_of(static_cast<int>(lo), i);
-            }
-            factor = s1 / 254.0f * a.qk_scale;
-        }
-        const int d = lane * 4;
-        auto offset = [&](int n) { return (n >> 3) * 1024 + (d >> 4) * 128 + (n & 7) * 16 + (d & 15); };
-        *reinterpret_cast<uint32_t*>(img + offset(r)) = hi_word;
-        *reinterpret_cast<uint32_t*>(img + offset(RMAX + r)) = lo_word;
-        if (lane == 0) factors[r] = factor;
     }
 }
 
@@ -713,8 +776,8 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(TcArgs t, int32_t* fir
         int32_t n = 0;
         if (b < a.batch) {
             const int64_t T = __ldg(a.context_lens + b);
-            const bool valid = T >= a.window && T <= a.table_stride * a.pool.block_size &&
-                               T <= a.max_chunks * a.chunk;
+            const bool valid =
+                T >= a.window && T <= a.table_stride * a.pool.block_size && T <= a.max_chunks * a.chunk;
             if (!valid) report_fault(a.status, SDC_FAULT_CONTEXT_RANGE);
             n = valid ? static_cast<int32_t>(((T + a.chunk - 1) / a.chunk) * a.kv_heads) : 0;
         }
@@ -765,12 +828,14 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// 2-D map over the pool's codes as rows of 128 bytes; one box = one page
+// (block_size rows), 128-byte swizzle to match the MMA operand layout.
 bool make_page_map(CUtensorMap* map, const int8_t* codes, const Pool& p) {
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return false;
     const int64_t last = (p.num_blocks - 1) * p.cbs + (p.num_layers - 1) * p.cls + (p.num_heads - 1) * p.chs;
     const uint64_t rows = static_cast<uint64_t>(last / kHeadDim + p.block_size);
-    if (rows > (uint64_t(1) << 32)) return false;
+    if (rows > (uint64_t(1) << 31)) return false;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHeadDim)};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(kHeadDim), static_cast<cuuint32_t>(p.block_size)};
@@ -780,12 +845,16 @@ bool make_page_map(CUtensorMap* map, const int8_t* codes, const Pool& p) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int rmax_for(int64_t rows) {
+// Row buckets with a compiled kernel; rows are padded up to the bucket.
+int bucket_for(int64_t rows) {
+    if (rows <= 0) return 0;
+    if (rows <= 8) return 8;
+    if (rows <= 16) return 16;
+    if (rows <= 20) return 20;
     if (rows <= 24) return 24;
-    if (rows <= 40) return 40;
+    if (rows <= 32) return 32;
     return 0;
 }
-
 
 int num_sms() {
     static int sms = 0;
@@ -798,16 +867,12 @@ int num_sms() {
     return sms;
 }
 
-template <typename QT, int RMAX>
-sdc_status_t launch_typed(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap, int32_t* first,
-                          cudaStream_t st) {
-    constexpr int STAGES = kStagesFor<RMAX>;
-    constexpr int MINB = kMinBlocksFor<RMAX>;
-    using LY = Layout<RMAX, STAGES>;
-    const int64_t bh = t.a.batch * t.a.kv_heads;
-    query_image_kernel<QT, RMAX><<<static_cast<unsigned>(bh), 256, 0, st>>>(t);
+template <int RB>
+sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap, int32_t* first,
+                           cudaStream_t st) {
+    using LY = Rows<RB>;
     plan_items_kernel<<<1, 1024, 0, st>>>(t, first);
-    auto kernel = attn_tc_kernel<RMAX, STAGES, MINB>;
+    auto kernel = attn_tc_kernel<RB>;
     static bool configured = false;
     if (!configured) {
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::kDynamicSmem) !=
@@ -816,35 +881,29 @@ sdc_status_t launch_typed(const TcArgs& t, const CUtensorMap& kmap, const CUtens
         }
         configured = true;
     }
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, LY::kDynamicSmem) != cudaSuccess ||
-        per_sm < 1) {
-        return SDC_STATUS_CUDA_ERROR;
-    }
-    per_sm = per_sm > MINB ? MINB : per_sm;  // never more blocks per SM than tensor memory holds
-    const int64_t max_items = bh * t.a.max_chunks;
-    const int64_t grid = std::min<int64_t>(static_cast<int64_t>(num_sms()) * per_sm, max_items);
+    const int64_t max_items = t.a.batch * t.a.kv_heads * t.a.max_chunks;
+    const int64_t grid = std::min<int64_t>(num_sms(), max_items);
     kernel<<<static_cast<unsigned>(grid), kThreads, LY::kDynamicSmem, st>>>(kmap, vmap, t);
     return launch_status();
 }
 
 }  // namespace
 
-bool shape_supported(int64_t head_dim, int64_t rows) { return head_dim == kHeadDim && rmax_for(rows) != 0; }
+bool shape_supported(int64_t head_dim, int64_t rows) { return head_dim == kHeadDim && bucket_for(rows) != 0; }
 
 bool supports(const AttnArgs& a) {
     const Pool& p = a.pool;
     const int64_t bs = p.block_size;
-    return p.head_dim == kHeadDim && rmax_for(a.rows) != 0 && bs >= 8 && bs <= kTile && (kTile % bs) == 0 &&
+    return shape_supported(p.head_dim, a.rows) && bs >= 8 && bs <= kTile && (kTile % bs) == 0 &&
            p.cbs % kHeadDim == 0 && p.cls % kHeadDim == 0 && p.chs % kHeadDim == 0 && p.sbs % 4 == 0 &&
            p.sls % 4 == 0 && p.shs % 4 == 0 && (reinterpret_cast<uintptr_t>(p.key_scales) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(p.value_scales) & 15) == 0 && encode_fn() != nullptr;
 }
 
 int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len) {
-    // about four items per resident block when every sequence is at the
-    // maximum length; a multiple of the tile
-    const int64_t slots = static_cast<int64_t>(num_sms()) * 2 * 4;
+    // about four items per SM when every sequence is at the maximum length;
+    // a multiple of the tile
+    const int64_t slots = static_cast<int64_t>(num_sms()) * 4;
     int64_t c = (batch * kv_heads * max_context_len + slots - 1) / slots;
     c = (c + kTile - 1) / kTile * kTile;
     if (c < 512) c = 512;
@@ -853,26 +912,18 @@ int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len) {
 }
 
 size_t extra_workspace(int64_t batch, int64_t kv_heads, int64_t max_chunks, int64_t rows) {
-    const int rmax = rmax_for(rows);
-    const int64_t q_bytes = rmax == 24 ? Layout<24, kStagesFor<24>>::kQBytes : Layout<40, kStagesFor<40>>::kQBytes;
-    const int64_t bh = batch * kv_heads;
+    (void)rows;
     auto up = [](int64_t v) { return static_cast<size_t>((v + 255) / 256 * 256); };
-    return up(bh * q_bytes) + up(bh * max_chunks * static_cast<int64_t>(sizeof(WorkItem))) + up(16) + up(batch * 4);
+    return up(batch * kv_heads * max_chunks * static_cast<int64_t>(sizeof(WorkItem))) + up(16) + up(batch * 4);
 }
 
 sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
-    const int rmax = rmax_for(a.rows);
     auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
-    const int64_t q_bytes = rmax == 24 ? Layout<24, kStagesFor<24>>::kQBytes : Layout<40, kStagesFor<40>>::kQBytes;
-    const int64_t bh = a.batch * a.kv_heads;
     char* base = static_cast<char*>(extra);
     TcArgs t;
     t.a = a;
-    t.qimg = reinterpret_cast<const uint8_t*>(base);
-    t.q_bytes = static_cast<int32_t>(q_bytes);
-    base += up(bh * q_bytes);
     t.items = reinterpret_cast<const WorkItem*>(base);
-    base += up(bh * a.max_chunks * static_cast<int64_t>(sizeof(WorkItem)));
+    base += up(a.batch * a.kv_heads * a.max_chunks * static_cast<int64_t>(sizeof(WorkItem)));
     t.item_count = reinterpret_cast<const int32_t*>(base);
     base += up(16);
     int32_t* first = reinterpret_cast<int32_t*>(base);
@@ -882,19 +933,12 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
         return SDC_STATUS_CUDA_ERROR;
     }
     sdc_status_t rc;
-    switch (a.query_dtype) {
-        case SDC_DTYPE_BF16:
-            rc = rmax == 24 ? launch_typed<__nv_bfloat16, 24>(t, kmap, vmap, first, st)
-                            : launch_typed<__nv_bfloat16, 40>(t, kmap, vmap, first, st);
-            break;
-        case SDC_DTYPE_F16:
-            rc = rmax == 24 ? launch_typed<__half, 24>(t, kmap, vmap, first, st)
-                            : launch_typed<__half, 40>(t, kmap, vmap, first, st);
-            break;
-        case SDC_DTYPE_F32:
-            rc = rmax == 24 ? launch_typed<float, 24>(t, kmap, vmap, first, st)
-                            : launch_typed<float, 40>(t, kmap, vmap, first, st);
-            break;
+    switch (bucket_for(a.rows)) {
+        case 8: rc = launch_bucket<8>(t, kmap, vmap, first, st); break;
+        case 16: rc = launch_bucket<16>(t, kmap, vmap, first, st); break;
+        case 20: rc = launch_bucket<20>(t, kmap, vmap, first, st); break;
+        case 24: rc = launch_bucket<24>(t, kmap, vmap, first, st); break;
+        case 32: rc = launch_bucket<32>(t, kmap, vmap, first, st); break;
         default: return SDC_STATUS_UNSUPPORTED;
     }
     if (rc != SDC_STATUS_OK) return rc;
