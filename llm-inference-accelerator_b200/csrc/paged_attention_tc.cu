@@ -51,7 +51,6 @@ constexpr int kGroups = 2;                                       // softmax warp
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = (kProducerWarp + 2) * 32;
-constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // one second
 constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
 
 template <int RB>
@@ -98,11 +97,12 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ unsigned long long globaltimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
+// Timeouts count SM clock cycles: reading the cycle counter is cheap, unlike
+// the global nanosecond timer, so a spinning wait notices a completed phase
+// at once.  2^31 cycles is about one second at B200 clocks.
+constexpr long long kWaitLimitCycles = 1ll << 31;
+
+__device__ __forceinline__ long long cycles() { return clock64(); }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -133,11 +133,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                            int32_t* status) {
     if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long start = globaltimer();
+    const long long start = cycles();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer() - start > kWaitLimitNs) {
+        if (cycles() - start > kWaitLimitCycles) {
             *abort_flag = 1;
             report_fault(status, SDC_FAULT_WAIT_TIMEOUT);
             return false;
@@ -153,9 +153,9 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 
 // Wait used while winding down: bounded, ignores the abort flag.
 __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity) {
-    const unsigned long long start = globaltimer();
+    const long long start = cycles();
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - start > kWaitLimitNs) return;
+        if (cycles() - start > kWaitLimitCycles) return;
     }
 }
 
@@ -390,8 +390,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int32_t* table = a.block_tables + static_cast<int64_t>(it.b) * a.table_stride;
             const int64_t code_base = a.layer * a.pool.cls + it.h * a.pool.chs;
             const int64_t scale_base = a.layer * a.pool.sls + it.h * a.pool.shs;
+            // lane j owns page j of a tile; its block id is fetched one tile
+            // ahead so the table load overlaps the wait for a free stage
+            auto page_of = [&](int tile0) -> int64_t {
+                const int64_t page_token = tile0 + static_cast<int64_t>(lane) * bs;
+                if (lane >= pages_per_tile || page_token >= it.t1) return -1;
+                return __ldg(table + page_token / bs);
+            };
+            int64_t next_blk = page_of(it.t0);
             bool stop = false;
             for (int tile0 = it.t0; tile0 < it.t1; tile0 += kTile, ++g) {
+                const int64_t blk = next_blk;
+                if (tile0 + kTile < it.t1) next_blk = page_of(tile0 + kTile);
                 const uint32_t s = g % STAGES;
                 if (!warp_wait(bar(kvEmpty + s), ((g / STAGES) & 1) ^ 1, abort_flag, a.status)) {
                     stop = true;
@@ -399,13 +409,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const int64_t page_token = tile0 + static_cast<int64_t>(lane) * bs;
                 bool valid = lane < pages_per_tile && page_token < it.t1;
-                int64_t blk = 0;
-                if (valid) {
-                    blk = __ldg(table + page_token / bs);
-                    if (blk < 0 || blk >= a.pool.num_blocks) {
-                        report_fault(a.status, SDC_FAULT_BLOCK_RANGE);
-                        valid = false;
-                    }
+                if (valid && (blk < 0 || blk >= a.pool.num_blocks)) {
+                    report_fault(a.status, SDC_FAULT_BLOCK_RANGE);
+                    valid = false;
                 }
                 const uint32_t mask = __ballot_sync(kFullMask, valid);
                 const uint32_t page_bytes = static_cast<uint32_t>(bs) * (2 * kHeadDim + 8);
