@@ -21,11 +21,14 @@
 // from HBM to shared memory exactly once, one TMA box per page, and is never
 // converted.
 //
-// Warp roles (320 threads, one block per SM): two softmax warpgroups take
-// alternate tiles (warpgroup k owns S/P/O buffer k; a thread is a token row of
-// S^T and a head_dim row of O^T, its TMEM lane), each with its own online
-// softmax state, merged at the end of an item; warp 8 quantizes the query
-// rows and issues TMA; warp 9 allocates tensor memory and issues the MMAs.
+// The planning launch quantizes every (sequence, KV head)'s query rows once;
+// items of the same pair share that image.  Warp roles of the item kernel
+// (352 threads, one block per SM): two softmax warpgroups take alternate
+// tiles (warpgroup k owns S/P/O buffer k; a thread is a token row of S^T and
+// a head_dim row of O^T, its TMEM lane), each with its own online softmax
+// state, merged at the end of an item; warp 8 copies the query image and the
+// key side of the pages, warp 10 the value side; warp 9 allocates tensor
+// memory and issues the MMAs.
 // Every mbarrier wait gives up after one second, records
 // SDC_FAULT_WAIT_TIMEOUT in the status word, and lets the block wind down:
 // it waits (bounded) for its own copies and MMAs, frees tensor memory and
@@ -48,9 +51,10 @@ constexpr int kHeadDim = 128;  // MMA M for O^T, and the K extent of S^T
 constexpr int kCodeTileBytes = kTile * kHeadDim;                 // 16 KiB
 constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;  // K, V codes + scales
 constexpr int kGroups = 2;                                       // softmax warpgroups
-constexpr int kProducerWarp = 8;
+constexpr int kProducerWarp = 8;  // query image + key side of every page
 constexpr int kMmaWarp = 9;
-constexpr int kThreads = (kProducerWarp + 2) * 32;
+constexpr int kValueWarp = 10;  // value side of every page
+constexpr int kThreads = 11 * 32;
 constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
 
 template <int RB>
@@ -58,14 +62,18 @@ struct Rows {
     static constexpr int N = ((2 * RB + 15) / 16) * 16;  // MMA N
     static constexpr int kStages = RB <= 24 ? 5 : 4;
     static constexpr int kQCodes = N * kHeadDim;
+    // one query image: the codes, then the RB row factors; global images
+    // are kQStride bytes apart, shared-memory buffers kQBufBytes
+    static constexpr int kQCopyBytes = kQCodes + RB * 4;
+    static constexpr int kQStride = ((kQCopyBytes + 127) / 128) * 128;
+    static constexpr int kQBufBytes = ((kQCopyBytes + 1023) / 1024) * 1024;
     static constexpr int kPBytes = N * kTile;
     static constexpr int kTmemStride = N <= 64 ? 64 : 128;  // columns per S / O buffer
     static constexpr int kTmemCols = 4 * kTmemStride;       // S0 S1 O0 O1
     // shared-memory offsets from a 1024-aligned base
     static constexpr int kStageOff = 0;
-    static constexpr int kQOff = kStages * kStageBytes;                           // 2 query images
-    static constexpr int kQFacOff = kQOff + 2 * kQCodes;                          // [2][RB] row factors
-    static constexpr int kPOff = ((kQFacOff + 2 * RB * 4 + 1023) / 1024) * 1024;  // 2 P tiles
+    static constexpr int kQOff = kStages * kStageBytes;  // 2 query images
+    static constexpr int kPOff = kQOff + 2 * kQBufBytes;  // 2 P tiles
     static constexpr int kRedOff = kPOff + 2 * kPBytes;  // [group][parity][warp][RB + 1]
     static constexpr int kAlphaOff = kRedOff + kGroups * 2 * 4 * (RB + 1) * 4;  // [group][parity][RB]
     static constexpr int kChgOff = kAlphaOff + kGroups * 2 * RB * 4;            // [group][parity] u32
@@ -78,16 +86,28 @@ struct Rows {
     static constexpr int kTotal = kMiscOff + 16;
     static constexpr int kDynamicSmem = kTotal + 1024;
     static_assert(RB <= 32, "row masks are 32 bits");
+    static_assert(RB % 4 == 0, "row factors fill whole 16-byte words");
 };
 
-struct WorkItem {
-    int32_t b, h, t0, t1;
+// Bytes between two (sequence, KV head) query images for row bucket rb.
+constexpr int64_t query_image_stride(int rb) {
+    return ((((2 * rb + 15) / 16) * 16 * kHeadDim + rb * 4 + 127) / 128) * 128;
+}
+
+// One unit of work: tokens [t0, t1) of sequence b (context length ctx) for
+// KV head h; chunk = t0 / chunk size, the partial's slot.
+struct __align__(32) WorkItem {
+    int32_t b, h, t0, t1, ctx, chunk, pad0, pad1;
 };
 
 struct TcArgs {
     AttnArgs a;
     const WorkItem* items;
     const int32_t* item_count;
+    // per (sequence, KV head): the query rows split into INT8 hi / lo parts
+    // in the score MMA's B layout, then the row factors (written by the
+    // planning launch)
+    unsigned char* qimg;
     int32_t rows;  // query rows per KV head (<= RB)
 };
 
@@ -280,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(bar(kvFull + s), 1);
+            mbar_init(bar(kvFull + s), 2);  // key-side and value-side producers
             mbar_init(bar(kvEmpty + s), 1 + 4);  // MMA commit + the consuming warpgroup
         }
         for (int i = 0; i < 2; ++i) {
@@ -297,10 +317,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar(mergeEmpty), 4);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    // query images: rows past `rows` stay zero for the whole kernel
-    for (int i = threadIdx.x; i < 2 * LY::kQCodes / 16; i += blockDim.x) {
-        reinterpret_cast<uint4*>(smem + LY::kQOff)[i] = make_uint4(0u, 0u, 0u, 0u);
     }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -321,81 +337,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t bs = a.pool.block_size;
     const int pages_per_tile = static_cast<int>(kTile / bs);
 
-    if (warp == kProducerWarp) {
-        // ------------------------------------------------------------ query rows + TMA
-        uint32_t g = 0, li = 0;
+    if (warp == kProducerWarp || warp == kValueWarp) {
+        // ------------------------------------------------------------ copies
+        // Warp 8 fetches each item's query image and the key codes and key
+        // scales of every page, warp 10 the value side; lane j owns page j of
+        // a tile.  Both arrive on the stage's full barrier with their bytes.
+        const bool key_side = warp == kProducerWarp;
+        const CUtensorMap* map = key_side ? &kmap : &vmap;
+        const float* scales = key_side ? a.pool.key_scales : a.pool.value_scales;
+        const uint32_t code_dst = (key_side ? 0u : static_cast<uint32_t>(kCodeTileBytes)) +
+                                  static_cast<uint32_t>(lane * bs * kHeadDim);
+        const uint32_t scale_dst = 2 * kCodeTileBytes + (key_side ? 0u : static_cast<uint32_t>(kTile * 4)) +
+                                   static_cast<uint32_t>(lane * bs * 4);
+        const uint32_t page_bytes = static_cast<uint32_t>(bs) * (kHeadDim + 4);
+        const int lg_bs = __ffs(static_cast<int>(bs)) - 1;  // block sizes are powers of two
+        uint32_t g = 0, li = 0, q_issued = 0;
+        WorkItem nxt = t.items[blockIdx.x];
         for (int item = blockIdx.x; item < count; item += gridDim.x, ++li) {
-            const WorkItem it = t.items[item];
-            const uint32_t qb = li & 1;
-            if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status)) break;
-            {
-                // Split each query row into INT8 hi / lo parts, laid out as the
-                // B operand of the score MMA (K-major, no swizzle: 8 rows x 16
-                // bytes per 128-byte core matrix, 16-byte K chunks 128 bytes
-                // apart, 8-row groups 1024 bytes apart).
-                const int64_t qrow0 = (static_cast<int64_t>(it.b) * a.query_heads + it.h * a.group) * a.window;
-                unsigned char* img = smem + LY::kQOff + qb * LY::kQCodes;
-                float* fac = reinterpret_cast<float*>(smem + LY::kQFacOff) + qb * RB;
-                const int d = lane * 4;
-                for (int r = 0; r < R; ++r) {
-                    float x[4];
-                    const int64_t e = (qrow0 + r) * kHeadDim + d;
-                    if (a.query_dtype == SDC_DTYPE_BF16) {
-                        const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.query) + e);
-                        x[0] = __uint_as_float(w.x << 16);
-                        x[1] = __uint_as_float(w.x & 0xffff0000u);
-                        x[2] = __uint_as_float(w.y << 16);
-                        x[3] = __uint_as_float(w.y & 0xffff0000u);
-                    } else if (a.query_dtype == SDC_DTYPE_F16) {
-                        const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const __half*>(a.query) + e);
-                        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
-                        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
-                        x[0] = lo.x;
-                        x[1] = lo.y;
-                        x[2] = hi.x;
-                        x[3] = hi.y;
-                    } else {
-                        const float4 w = *reinterpret_cast<const float4*>(static_cast<const float*>(a.query) + e);
-                        x[0] = w.x;
-                        x[1] = w.y;
-                        x[2] = w.z;
-                        x[3] = w.w;
-                    }
-                    float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-#pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
-                    uint32_t hi_word = 0, lo_word = 0;
-                    float factor = 0.0f;
-                    if (m > 0.0f) {
-                        const float s1 = m / 127.0f;
-                        const float inv = 1.0f / s1;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float hi = fminf(fmaxf(rintf(x[i] * inv), -127.0f), 127.0f);
-                            const float lo = fminf(fmaxf(rintf((x[i] - hi * s1) * (254.0f * inv)), -127.0f), 127.0f);
-                            hi_word |= (static_cast<uint32_t>(static_cast<int>(hi)) & 0xffu) << (8 * i);
-                            lo_word |= (static_cast<uint32_t>(static_cast<int>(lo)) & 0xffu) << (8 * i);
-                        }
-                        factor = s1 / 254.0f * a.qk_scale;
-                    }
-                    auto offset = [&](int n) { return (n >> 3) * 1024 + (d >> 4) * 128 + (n & 7) * 16 + (d & 15); };
-                    *reinterpret_cast<uint32_t*>(img + offset(r)) = hi_word;
-                    *reinterpret_cast<uint32_t*>(img + offset(RB + r)) = lo_word;
-                    if (lane == 0) fac[r] = factor;
+            const WorkItem it = nxt;
+            if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
+            if (key_side) {
+                const uint32_t qb = li & 1;
+                if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status)) break;
+                if (lane == 0) {
+                    const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
+                    mbar_arrive_expect_tx(bar(qFull + qb), LY::kQCopyBytes);
+                    bulk_load(q_base + qb * LY::kQBufBytes, t.qimg + bh * LY::kQStride, LY::kQCopyBytes,
+                              bar(qFull + qb));
                 }
-                fence_proxy_async();  // the tensor core reads the image through the async proxy
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(qFull + qb));
+                ++q_issued;
             }
             const int32_t* table = a.block_tables + static_cast<int64_t>(it.b) * a.table_stride;
             const int64_t code_base = a.layer * a.pool.cls + it.h * a.pool.chs;
             const int64_t scale_base = a.layer * a.pool.sls + it.h * a.pool.shs;
-            // lane j owns page j of a tile; its block id is fetched one tile
-            // ahead so the table load overlaps the wait for a free stage
+            // a page's block id is fetched one tile ahead, so the table load
+            // overlaps the wait for a free stage
             auto page_of = [&](int tile0) -> int64_t {
-                const int64_t page_token = tile0 + static_cast<int64_t>(lane) * bs;
-                if (lane >= pages_per_tile || page_token >= it.t1) return -1;
-                return __ldg(table + page_token / bs);
+                const int page = (tile0 >> lg_bs) + lane;
+                if (lane >= pages_per_tile || (page << lg_bs) >= it.t1) return -1;
+                return __ldg(table + page);
             };
             int64_t next_blk = page_of(it.t0);
             bool stop = false;
@@ -407,28 +388,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     stop = true;
                     break;
                 }
-                const int64_t page_token = tile0 + static_cast<int64_t>(lane) * bs;
-                bool valid = lane < pages_per_tile && page_token < it.t1;
+                bool valid = lane < pages_per_tile && tile0 + (lane << lg_bs) < it.t1;
                 if (valid && (blk < 0 || blk >= a.pool.num_blocks)) {
-                    report_fault(a.status, SDC_FAULT_BLOCK_RANGE);
+                    if (key_side) report_fault(a.status, SDC_FAULT_BLOCK_RANGE);
                     valid = false;
                 }
                 const uint32_t mask = __ballot_sync(kFullMask, valid);
-                const uint32_t page_bytes = static_cast<uint32_t>(bs) * (2 * kHeadDim + 8);
                 if (lane == 0) mbar_arrive_expect_tx(bar(kvFull + s), __popc(mask) * page_bytes);
                 __syncwarp();
                 if (valid) {
                     const uint32_t st = stage_base + s * kStageBytes;
                     const int32_t row = static_cast<int32_t>((blk * a.pool.cbs + code_base) / kHeadDim);
-                    const uint32_t dst = static_cast<uint32_t>(lane * bs * kHeadDim);
-                    tma_load_2d(st + dst, &kmap, 0, row, bar(kvFull + s));
-                    tma_load_2d(st + kCodeTileBytes + dst, &vmap, 0, row, bar(kvFull + s));
-                    const int64_t scale_off = blk * a.pool.sbs + scale_base;
-                    const uint32_t sdst = static_cast<uint32_t>(lane * bs * 4);
-                    bulk_load(st + 2 * kCodeTileBytes + sdst, a.pool.key_scales + scale_off,
-                              static_cast<uint32_t>(bs * 4), bar(kvFull + s));
-                    bulk_load(st + 2 * kCodeTileBytes + kTile * 4 + sdst, a.pool.value_scales + scale_off,
-                              static_cast<uint32_t>(bs * 4), bar(kvFull + s));
+                    tma_load_2d(st + code_dst, map, 0, row, bar(kvFull + s));
+                    bulk_load(st + scale_dst, scales + blk * a.pool.sbs + scale_base, static_cast<uint32_t>(bs * 4),
+                              bar(kvFull + s));
                 }
             }
             if (stop) break;
@@ -437,6 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t k = 0; k < STAGES && k < g; ++k) {
                 const uint32_t gg = g - 1 - k;
                 drain_phase(bar(kvFull + gg % STAGES), (gg / STAGES) & 1);
+            }
+            for (uint32_t k = 0; k < 2 && k < q_issued; ++k) {
+                const uint32_t lq = q_issued - 1 - k;
+                drain_phase(bar(qFull + (lq & 1)), (lq >> 1) & 1);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -470,8 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             return true;
         };
         bool ok = true;
+        WorkItem nxt = t.items[blockIdx.x];
         for (int item = blockIdx.x; item < count && ok; item += gridDim.x, ++li) {
-            const WorkItem it = t.items[item];
+            const WorkItem it = nxt;
+            if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
             const uint32_t qb = li & 1;
             if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status)) break;
             for (int tile0 = it.t0; tile0 < it.t1; tile0 += kTile, ++g) {
@@ -485,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t k_tile = stage_base + s * kStageBytes;
-                    const uint32_t q_tile = q_base + qb * LY::kQCodes;
+                    const uint32_t q_tile = q_base + qb * LY::kQBufBytes;
 #pragma unroll
                     for (int ks = 0; ks < kHeadDim / 32; ++ks) {
                         const uint64_t da = smem_desc(k_tile + ks * 32, 16, 1024, 2);
@@ -563,12 +542,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
 
         bool ok = true;
+        WorkItem nxt = t.items[blockIdx.x];
         for (int item = blockIdx.x; item < count && ok; item += gridDim.x, ++li) {
-            const WorkItem it = t.items[item];
+            const WorkItem it = nxt;
+            if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
             const uint32_t qb = li & 1;
             if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status)) break;
-            const float* qfac = reinterpret_cast<const float*>(smem + LY::kQFacOff) + qb * RB;
-            const int64_t T = __ldg(a.context_lens + it.b);
+            const float* qfac = reinterpret_cast<const float*>(smem + LY::kQOff + qb * LY::kQBufBytes + LY::kQCodes);
+            const int64_t T = it.ctx;
             const int64_t window = a.window;
             float m_lane = -INFINITY;  // lane r holds the running max of row r
             float l_thr[RB], o_acc[RB];
@@ -738,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     l_tot = l_lane * e0_lane + l1 * e1_lane;
                 }
                 const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
-                const int64_t chunk = it.t0 / a.chunk;
+                const int64_t chunk = it.chunk;
                 float* part_o = a.part_o + (bh * a.max_chunks + chunk) * R * kHeadDim;
                 float* part_ml = a.part_ml + (bh * a.max_chunks + chunk) * R * 2;
 #pragma unroll
@@ -768,13 +749,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// Work list: (sequence, KV head, chunk) items, sequences in order; sequences
-// whose context length is invalid get no items (the combine writes zeros).
-__global__ void __launch_bounds__(1024) plan_items_kernel(TcArgs t, int32_t* first) {
+// Planning launch.  Block 0 writes the work list: (sequence, KV head, chunk)
+// items, sequences in order; sequences whose context length is invalid get
+// no items (the combine writes zeros).  Every other block quantizes query
+// rows, one warp per (sequence, KV head, row): each row splits into INT8
+// hi / lo parts written in the score MMA's B layout (K-major, no swizzle:
+// 8 rows x 16 bytes per 128-byte core matrix, 16-byte K chunks 128 bytes
+// apart, 8-row groups 1024 bytes apart), and its factor s1 / 254 * qk_scale.
+// Rows past `rows`, and the padding rows of the MMA's N, are zero.
+template <int RB>
+__global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
+    using LY = Rows<RB>;
+    const AttnArgs& a = t.a;
+    if (blockIdx.x > 0) {
+        const int lane = threadIdx.x & 31;
+        const int64_t w = static_cast<int64_t>(blockIdx.x - 1) * 32 + (threadIdx.x >> 5);
+        const int64_t bh = w / RB;
+        const int r = static_cast<int>(w - bh * RB);
+        if (bh >= a.batch * a.kv_heads) return;
+        const int64_t b = bh / a.kv_heads;
+        const int64_t h = bh - b * a.kv_heads;
+        unsigned char* img = t.qimg + bh * LY::kQStride;
+        const int d = lane * 4;
+        float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (r < t.rows) {
+            const int64_t e = ((b * a.query_heads + h * a.group) * a.window + r) * kHeadDim + d;
+            if (a.query_dtype == SDC_DTYPE_BF16) {
+                const uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.query) + e));
+                x[0] = __uint_as_float(v.x << 16);
+                x[1] = __uint_as_float(v.x & 0xffff0000u);
+                x[2] = __uint_as_float(v.y << 16);
+                x[3] = __uint_as_float(v.y & 0xffff0000u);
+            } else if (a.query_dtype == SDC_DTYPE_F16) {
+                const uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const __half*>(a.query) + e));
+                const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+                const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+                x[0] = lo.x;
+                x[1] = lo.y;
+                x[2] = hi.x;
+                x[3] = hi.y;
+            } else {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.query) + e));
+                x[0] = v.x;
+                x[1] = v.y;
+                x[2] = v.z;
+                x[3] = v.w;
+            }
+        }
+        float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, off));
+        uint32_t hi_word = 0, lo_word = 0;
+        float factor = 0.0f;
+        if (m > 0.0f) {
+            const float s1 = m / 127.0f;
+            const float inv = 1.0f / s1;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float hi = fminf(fmaxf(rintf(x[i] * inv), -127.0f), 127.0f);
+                const float lo = fminf(fmaxf(rintf((x[i] - hi * s1) * (254.0f * inv)), -127.0f), 127.0f);
+                hi_word |= (static_cast<uint32_t>(static_cast<int>(hi)) & 0xffu) << (8 * i);
+                lo_word |= (static_cast<uint32_t>(static_cast<int>(lo)) & 0xffu) << (8 * i);
+            }
+            factor = s1 / 254.0f * a.qk_scale;
+        }
+        auto offset = [&](int n) { return (n >> 3) * 1024 + (d >> 4) * 128 + (n & 7) * 16 + (d & 15); };
+        *reinterpret_cast<uint32_t*>(img + offset(r)) = hi_word;
+        *reinterpret_cast<uint32_t*>(img + offset(RB + r)) = lo_word;
+        if (2 * RB + r < LY::N) *reinterpret_cast<uint32_t*>(img + offset(2 * RB + r)) = 0u;
+        if (lane == 0) reinterpret_cast<float*>(img + LY::kQCodes)[r] = factor;
+        return;
+    }
+
     using Scan = cub::BlockScan<int32_t, 1024>;
     __shared__ typename Scan::TempStorage temp;
     __shared__ int32_t carry;
-    const AttnArgs& a = t.a;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
     for (int64_t base = 0; base < a.batch; base += 1024) {
@@ -808,6 +857,9 @@ __global__ void __launch_bounds__(1024) plan_items_kernel(TcArgs t, int32_t* fir
                 w.h = static_cast<int32_t>(h);
                 w.t0 = static_cast<int32_t>(c * a.chunk);
                 w.t1 = static_cast<int32_t>(min(T, (c + 1) * a.chunk));
+                w.ctx = static_cast<int32_t>(T);
+                w.chunk = static_cast<int32_t>(c);
+                w.pad0 = w.pad1 = 0;
                 out[c * a.kv_heads + h] = w;
             }
         }
@@ -877,7 +929,8 @@ template <int RB>
 sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap, int32_t* first,
                            cudaStream_t st) {
     using LY = Rows<RB>;
-    plan_items_kernel<<<1, 1024, 0, st>>>(t, first);
+    const int64_t query_warps = t.a.batch * t.a.kv_heads * RB;
+    prep_kernel<RB><<<static_cast<unsigned>(1 + (query_warps + 31) / 32), 1024, 0, st>>>(t, first);
     auto kernel = attn_tc_kernel<RB>;
     static bool configured = false;
     if (!configured) {
@@ -918,9 +971,9 @@ int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len) {
 }
 
 size_t extra_workspace(int64_t batch, int64_t kv_heads, int64_t max_chunks, int64_t rows) {
-    (void)rows;
     auto up = [](int64_t v) { return static_cast<size_t>((v + 255) / 256 * 256); };
-    return up(batch * kv_heads * max_chunks * static_cast<int64_t>(sizeof(WorkItem))) + up(16) + up(batch * 4);
+    return up(batch * kv_heads * max_chunks * static_cast<int64_t>(sizeof(WorkItem))) + up(16) + up(batch * 4) +
+           up(batch * kv_heads * query_image_stride(bucket_for(rows)));
 }
 
 sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
@@ -933,6 +986,8 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
     t.item_count = reinterpret_cast<const int32_t*>(base);
     base += up(16);
     int32_t* first = reinterpret_cast<int32_t*>(base);
+    base += up(a.batch * 4);
+    t.qimg = reinterpret_cast<unsigned char*>(base);
     t.rows = static_cast<int32_t>(a.rows);
     CUtensorMap kmap, vmap;
     if (!make_page_map(&kmap, a.pool.keys, a.pool) || !make_page_map(&vmap, a.pool.values, a.pool)) {
