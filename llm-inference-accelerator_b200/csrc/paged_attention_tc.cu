@@ -73,18 +73,20 @@ struct Rows {
     // shared-memory offsets from a 1024-aligned base
     static constexpr int kStageOff = 0;
     static constexpr int kQOff = kStages * kStageBytes;  // 2 query images
-    static constexpr int kPOff = kQOff + 2 * kQBufBytes;  // 2 P tiles
-    static constexpr int kRedOff = kPOff + 2 * kPBytes;  // [group][parity][warp][RB + 1]
+    static constexpr int kPOff = kQOff + 2 * kQBufBytes;  // [group][own tile parity] P tiles
+    static constexpr int kRedOff = kPOff + 4 * kPBytes;   // [group][parity][warp][RB + 1]
     static constexpr int kAlphaOff = kRedOff + kGroups * 2 * 4 * (RB + 1) * 4;  // [group][parity][RB]
     static constexpr int kChgOff = kAlphaOff + kGroups * 2 * RB * 4;            // [group][parity] u32
     static constexpr int kVfacOff = kChgOff + kGroups * 2 * 4;                  // [group][parity]
     static constexpr int kMergeOOff = kVfacOff + kGroups * 2 * 4;               // [128][RB]
     static constexpr int kMergeMLOff = kMergeOOff + 128 * RB * 4;               // [RB][2]
     static constexpr int kBarOff = ((kMergeMLOff + RB * 8 + 7) / 8) * 8;
-    static constexpr int kNumBars = 2 * kStages + 2 * 7 + 2 * kGroups + 2;
+    static constexpr int kNumBars = 2 * kStages + 2 * 7 + 2 + 2 * kGroups + 2;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-    static constexpr int kTotal = kMiscOff + 16;
+    static constexpr int kCausalOff = kMiscOff + 16;  // [32] row masks of the causal window
+    static constexpr int kTotal = kCausalOff + 32 * 4;
     static constexpr int kDynamicSmem = kTotal + 1024;
+    static_assert(kDynamicSmem <= 232448, "shared memory per block");
     static_assert(RB <= 32, "row masks are 32 bits");
     static_assert(RB % 4 == 0, "row factors fill whole 16-byte words");
 };
@@ -134,6 +136,19 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Non-blocking probe of a phase (polling loops).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -293,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kBarOff);
     auto bar = [&](int i) { return smem_u32(bars + i); };
     const int kvFull = 0, kvEmpty = STAGES, qFull = 2 * STAGES, qEmpty = qFull + 2, sFull = qEmpty + 2,
-              sEmpty = sFull + 2, pFull = sEmpty + 2, oFull = pFull + 2, oEmpty = oFull + 2,
+              sEmpty = sFull + 2, pFull = sEmpty + 2 /* [group][P tile] */, oFull = pFull + 4, oEmpty = oFull + 2,
               xch = oEmpty + 2 /* [group][parity] */, mergeFull = xch + 2 * kGroups, mergeEmpty = mergeFull + 1;
     volatile uint32_t* tmem_base_slot = reinterpret_cast<volatile uint32_t*>(smem + LY::kMiscOff);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::kMiscOff + 4);
@@ -308,7 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar(qEmpty + i), 1 + 4 * kGroups);
             mbar_init(bar(sFull + i), 1);
             mbar_init(bar(sEmpty + i), 4);
-            mbar_init(bar(pFull + i), 128);
+            mbar_init(bar(pFull + 2 * i), 128);
+            mbar_init(bar(pFull + 2 * i + 1), 128);
             mbar_init(bar(oFull + i), 1);
             mbar_init(bar(oEmpty + i), 4);
         }
@@ -317,6 +333,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar(mergeEmpty), 4);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < 32) {
+        // causal[j]: the rows a key j positions past the last fully visible
+        // one stays visible to (row r = group row * window + i sees i >= j)
+        uint32_t m = 0;
+        for (int r = 0; r < t.rows; ++r) {
+            if (r % a.window >= static_cast<int>(threadIdx.x)) m |= 1u << r;
+        }
+        reinterpret_cast<uint32_t*>(smem + LY::kCausalOff)[threadIdx.x] = m;
     }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -418,79 +443,103 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
+        // One thread issues both products as soon as their inputs are ready:
+        // the score MMA of tile gs needs its stage, its S buffer (released
+        // once the owning warpgroup has read S of tile gs - 2) and its item's
+        // query image; the P.V MMA of tile gp needs P of tile gp and its O
+        // buffer.  Scores therefore run ahead of P.V instead of queueing
+        // behind it.  Both waits are polled; the thread gives up after
+        // kWaitLimitCycles without progress.
         constexpr uint32_t kIdescS = idesc_i8(kTile, N, 0, 0);
         constexpr uint32_t kIdescO = idesc_i8(kHeadDim, N, 1, 1);
-        uint32_t g = 0, li = 0;
-        bool have_prev = false, any_s = false, any_o = false;
-        uint32_t prev = 0, last_s = 0, last_o = 0;
-        auto issue_pv = [&](uint32_t gp) -> bool {
-            const uint32_t sb = gp & 1;
-            const uint32_t s = gp % STAGES;
-            if (!warp_wait(bar(pFull + sb), (gp >> 1) & 1, abort_flag, a.status)) return false;
-            if (!warp_wait(bar(oEmpty + sb), ((gp >> 1) & 1) ^ 1, abort_flag, a.status)) return false;
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t v_tile = stage_base + s * kStageBytes + kCodeTileBytes;
-                const uint32_t p_tile = p_base + sb * LY::kPBytes;
-#pragma unroll
-                for (int ks = 0; ks < kTile / 32; ++ks) {
-                    const uint64_t da = smem_desc(v_tile + ks * 4096, kCodeTileBytes, 1024, 2);
-                    const uint64_t db = smem_desc(p_tile + ks * 512, 128, 2048, 0);
-                    mma_i8(tmem + (2 + sb) * LY::kTmemStride, da, db, kIdescO, ks > 0);
-                }
-                mma_commit(bar(oFull + sb));
-                mma_commit(bar(kvEmpty + s));
-            }
-            __syncwarp();
-            last_o = gp;
-            any_o = true;
-            return true;
-        };
-        bool ok = true;
-        WorkItem nxt = t.items[blockIdx.x];
-        for (int item = blockIdx.x; item < count && ok; item += gridDim.x, ++li) {
-            const WorkItem it = nxt;
+        if (lane == 0) {
+            uint32_t gs = 0, gp = 0, li = 0;
+            int item = blockIdx.x;
+            WorkItem it = t.items[item];
+            WorkItem nxt = it;
             if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
-            const uint32_t qb = li & 1;
-            if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status)) break;
-            for (int tile0 = it.t0; tile0 < it.t1; tile0 += kTile, ++g) {
-                const uint32_t s = g % STAGES;
-                const uint32_t sb = g & 1;
-                if (!warp_wait(bar(kvFull + s), (g / STAGES) & 1, abort_flag, a.status) ||
-                    !warp_wait(bar(sEmpty + sb), ((g >> 1) & 1) ^ 1, abort_flag, a.status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t k_tile = stage_base + s * kStageBytes;
-                    const uint32_t q_tile = q_base + qb * LY::kQBufBytes;
+            int tile0 = it.t0;
+            bool s_done = false, q_ready = false;
+            long long idle_since = cycles();
+            while (true) {
+                bool progress = false;
+                if (!s_done) {
+                    const uint32_t qb = li & 1;
+                    const uint32_t s = gs % STAGES;
+                    const uint32_t sb = gs & 1;
+                    if (!q_ready) q_ready = mbar_test(bar(qFull + qb), (li >> 1) & 1);
+                    if (q_ready && mbar_test(bar(kvFull + s), (gs / STAGES) & 1) &&
+                        mbar_test(bar(sEmpty + sb), ((gs >> 1) & 1) ^ 1)) {
+                        tc_fence_after();
+                        const uint32_t k_tile = stage_base + s * kStageBytes;
+                        const uint32_t q_tile = q_base + qb * LY::kQBufBytes;
 #pragma unroll
-                    for (int ks = 0; ks < kHeadDim / 32; ++ks) {
-                        const uint64_t da = smem_desc(k_tile + ks * 32, 16, 1024, 2);
-                        const uint64_t db = smem_desc(q_tile + ks * 256, 128, 1024, 0);
-                        mma_i8(tmem + sb * LY::kTmemStride, da, db, kIdescS, ks > 0);
+                        for (int ks = 0; ks < kHeadDim / 32; ++ks) {
+                            const uint64_t da = smem_desc(k_tile + ks * 32, 16, 1024, 2);
+                            const uint64_t db = smem_desc(q_tile + ks * 256, 128, 1024, 0);
+                            mma_i8(tmem + sb * LY::kTmemStride, da, db, kIdescS, ks > 0);
+                        }
+                        mma_commit(bar(sFull + sb));
+                        ++gs;
+                        progress = true;
+                        tile0 += kTile;
+                        if (tile0 >= it.t1) {  // the item's last tile: its query image is free once this lands
+                            mma_commit(bar(qEmpty + qb));
+                            item += gridDim.x;
+                            ++li;
+                            q_ready = false;
+                            if (item >= count) {
+                                s_done = true;
+                            } else {
+                                it = nxt;
+                                if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
+                                tile0 = it.t0;
+                            }
+                        }
                     }
-                    mma_commit(bar(sFull + sb));
-                    if (tile0 + kTile >= it.t1) mma_commit(bar(qEmpty + qb));
                 }
-                __syncwarp();
-                last_s = g;
-                any_s = true;
-                if (have_prev && !issue_pv(prev)) {
-                    ok = false;
-                    have_prev = false;
+                if (gp < gs) {
+                    const uint32_t sb = gp & 1;
+                    const uint32_t s = gp % STAGES;
+                    // P tile (gp >> 1) & 1 of the owning warpgroup: one phase per
+                    // two of its tiles, and its next phase needs this product
+                    // complete, so the parity cannot be a phase behind
+                    if (mbar_test(bar(pFull + sb * 2 + ((gp >> 1) & 1)), (gp >> 2) & 1) &&
+                        mbar_test(bar(oEmpty + sb), ((gp >> 1) & 1) ^ 1)) {
+                        tc_fence_after();
+                        const uint32_t v_tile = stage_base + s * kStageBytes + kCodeTileBytes;
+                        const uint32_t p_tile = p_base + (sb * 2 + ((gp >> 1) & 1)) * LY::kPBytes;
+#pragma unroll
+                        for (int ks = 0; ks < kTile / 32; ++ks) {
+                            const uint64_t da = smem_desc(v_tile + ks * 4096, kCodeTileBytes, 1024, 2);
+                            const uint64_t db = smem_desc(p_tile + ks * 512, 128, 2048, 0);
+                            mma_i8(tmem + (2 + sb) * LY::kTmemStride, da, db, kIdescO, ks > 0);
+                        }
+                        mma_commit(bar(oFull + sb));
+                        mma_commit(bar(kvEmpty + s));
+                        ++gp;
+                        progress = true;
+                    }
+                } else if (s_done) {
                     break;
                 }
-                prev = g;
-                have_prev = true;
+                if (progress) {
+                    idle_since = cycles();
+                } else {
+                    if (*abort_flag) break;
+                    if (cycles() - idle_since > kWaitLimitCycles) {
+                        *abort_flag = 1;
+                        report_fault(a.status, SDC_FAULT_WAIT_TIMEOUT);
+                        break;
+                    }
+                }
+            }
+            if (*abort_flag) {  // the MMAs issued have completed before tensor memory is freed
+                if (gs > 0) drain_phase(bar(sFull + ((gs - 1) & 1)), ((gs - 1) >> 1) & 1);
+                if (gp > 0) drain_phase(bar(oFull + ((gp - 1) & 1)), ((gp - 1) >> 1) & 1);
             }
         }
-        if (ok && have_prev) issue_pv(prev);
-        if (*abort_flag && lane == 0) {
-            if (any_s) drain_phase(bar(sFull + (last_s & 1)), (last_s >> 1) & 1);
-            if (any_o) drain_phase(bar(oFull + (last_o & 1)), (last_o >> 1) & 1);
-        }
+        __syncwarp();
     } else {
         // ------------------------------------------------------------ softmax + O epilogue
         // Warpgroup `grp` takes the tiles with g % 2 == grp.  Cross-warp data
@@ -551,6 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* qfac = reinterpret_cast<const float*>(smem + LY::kQOff + qb * LY::kQBufBytes + LY::kQCodes);
             const int64_t T = it.ctx;
             const int64_t window = a.window;
+            const uint32_t row_mask = R >= 32 ? 0xffffffffu : (1u << R) - 1u;
             float m_lane = -INFINITY;  // lane r holds the running max of row r
             float l_thr[RB], o_acc[RB];
 #pragma unroll
@@ -584,15 +634,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kvEmpty + s));
 
-                // a query at window row i sees keys up to T - window + i; only
-                // tiles reaching into the window need the per-row test
-                const bool causal_tile = tile0 + kTile > T - window;
+                // a query at window row i sees keys up to T - window + i
+                uint32_t vis_mask = tvalid ? row_mask : 0u;
+                const int64_t past = tok - (T - window);  // > 0: inside the window
+                if (past > 0) {
+                    vis_mask &= past < window ? reinterpret_cast<const uint32_t*>(smem + LY::kCausalOff)[past] : 0u;
+                }
                 float sc[RB];
                 float* red_x = red + (xc & 1) * 4 * (RB + 1);
 #pragma unroll
                 for (int r = 0; r < RB; ++r) {
-                    bool vis = tvalid && r < R;
-                    if (causal_tile) vis = vis && tok <= T - window + (r % window);
+                    const bool vis = (vis_mask >> r) & 1u;
                     const int32_t combined = static_cast<int32_t>(sreg[r]) * 254 + static_cast<int32_t>(sreg[RB + r]);
                     sc[r] = vis ? static_cast<float>(combined) * (qfac[r] * kscale) : -INFINITY;
                     const float wm = redux_max(sc[r]);
@@ -656,14 +708,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // P^T row of this token in the MN-major no-swizzle layout: a
                 // 128-byte core matrix holds 16 columns x 8 tokens; 8-token
                 // groups are 128 bytes apart, 16-column groups 2048 apart.
-                unsigned char* prow = smem + LY::kPOff + grp * LY::kPBytes + (tid >> 3) * 128 + (tid & 7) * 16;
+                // Two P tiles per warpgroup: P of own tile k is written once
+                // this warp's epilogue of own tile k - 2 has seen that tile's
+                // P.V product complete.
+                unsigned char* prow =
+                    smem + LY::kPOff + (grp * 2 + (own & 1)) * LY::kPBytes + (tid >> 3) * 128 + (tid & 7) * 16;
 #pragma unroll
                 for (int c = 0; c < N / 16; ++c) {
                     *reinterpret_cast<uint4*>(prow + c * 2048) =
                         make_uint4(words[4 * c], words[4 * c + 1], words[4 * c + 2], words[4 * c + 3]);
                 }
                 fence_proxy_async();
-                mbar_arrive(bar(pFull + grp));
+                mbar_arrive(bar(pFull + grp * 2 + (own & 1)));
 
                 if (have_prev && !epilogue(prev_own, o_acc)) {
                     ok = false;
