@@ -51,10 +51,11 @@ constexpr int kHeadDim = 128;  // MMA M for O^T, and the K extent of S^T
 constexpr int kCodeTileBytes = kTile * kHeadDim;                 // 16 KiB
 constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;  // K, V codes + scales
 constexpr int kGroups = 2;                                       // softmax warpgroups
-constexpr int kProducerWarp = 8;  // query image + key side of every page
+constexpr int kKeyWarp = 8;  // key codes of every page
 constexpr int kMmaWarp = 9;
-constexpr int kValueWarp = 10;  // value side of every page
-constexpr int kThreads = 11 * 32;
+constexpr int kValueWarp = 10;  // value codes of every page
+constexpr int kScaleWarp = 11;  // key and value scales of every page, query images
+constexpr int kThreads = 12 * 32;
 constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
 
 template <int RB>
@@ -74,11 +75,10 @@ struct Rows {
     static constexpr int kStageOff = 0;
     static constexpr int kQOff = kStages * kStageBytes;  // 2 query images
     static constexpr int kPOff = kQOff + 2 * kQBufBytes;  // [group][own tile parity] P tiles
-    static constexpr int kRedOff = kPOff + 4 * kPBytes;   // [group][parity][warp][RB + 1]
-    static constexpr int kAlphaOff = kRedOff + kGroups * 2 * 4 * (RB + 1) * 4;  // [group][parity][RB]
-    static constexpr int kChgOff = kAlphaOff + kGroups * 2 * RB * 4;            // [group][parity] u32
-    static constexpr int kVfacOff = kChgOff + kGroups * 2 * 4;                  // [group][parity]
-    static constexpr int kMergeOOff = kVfacOff + kGroups * 2 * 4;               // [128][RB]
+    static constexpr int kRedStride = RB + 4;            // RB row maxima, the value-scale maximum, padding
+    static constexpr int kRedOff = kPOff + 4 * kPBytes;   // [group][parity][warp][kRedStride]
+    static constexpr int kWarpOff = kRedOff + kGroups * 2 * 4 * kRedStride * 4;  // [warp][-m[RB], alpha[2][RB]]
+    static constexpr int kMergeOOff = kWarpOff + 2 * kGroups * 4 * 3 * RB * 4;   // [128][RB]
     static constexpr int kMergeMLOff = kMergeOOff + 128 * RB * 4;               // [RB][2]
     static constexpr int kBarOff = ((kMergeMLOff + RB * 8 + 7) / 8) * 8;
     static constexpr int kNumBars = 2 * kStages + 2 * 7 + 2 + 2 * kGroups + 2;
@@ -110,7 +110,8 @@ struct TcArgs {
     // in the score MMA's B layout, then the row factors (written by the
     // planning launch)
     unsigned char* qimg;
-    int32_t rows;  // query rows per KV head (<= RB)
+    int32_t rows;        // query rows per KV head (<= RB)
+    int32_t gather4;     // scales fetched four pages per copy through the scale maps
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -203,6 +204,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Four rows of a 2-D map (box one row high) at independent row coordinates,
+// stored back to back.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int32_t y0, int32_t y1, int32_t y2,
+                                            int32_t y3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
@@ -291,7 +303,8 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t w0, uint32_t w1, uin
 
 template <int RB>
 __global__ void __launch_bounds__(kThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, TcArgs t) {
+    attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   const __grid_constant__ CUtensorMap ksmap, const __grid_constant__ CUtensorMap vsmap, TcArgs t) {
     using LY = Rows<RB>;
     constexpr int N = LY::N;
     constexpr int STAGES = LY::kStages;
@@ -315,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(bar(kvFull + s), 2);  // key-side and value-side producers
+            mbar_init(bar(kvFull + s), 3);  // the three copy warps
             mbar_init(bar(kvEmpty + s), 1 + 4);  // MMA commit + the consuming warpgroup
         }
         for (int i = 0; i < 2; ++i) {
@@ -362,26 +375,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t bs = a.pool.block_size;
     const int pages_per_tile = static_cast<int>(kTile / bs);
 
-    if (warp == kProducerWarp || warp == kValueWarp) {
+    if (warp == kKeyWarp || warp == kValueWarp || warp == kScaleWarp) {
         // ------------------------------------------------------------ copies
-        // Warp 8 fetches each item's query image and the key codes and key
-        // scales of every page, warp 10 the value side; lane j owns page j of
-        // a tile.  Both arrive on the stage's full barrier with their bytes.
-        const bool key_side = warp == kProducerWarp;
-        const CUtensorMap* map = key_side ? &kmap : &vmap;
-        const float* scales = key_side ? a.pool.key_scales : a.pool.value_scales;
-        const uint32_t code_dst = (key_side ? 0u : static_cast<uint32_t>(kCodeTileBytes)) +
+        // Three warps share the copies of a tile, each arriving on the
+        // stage's full barrier with its own bytes: warp 8 the key codes and
+        // warp 10 the value codes (lane j copies page j), warp 11 the key and
+        // value scales (four pages per gather when a tile holds a multiple of
+        // four pages) and, once per item, the query image.
+        const bool scale_side = warp == kScaleWarp;
+        const CUtensorMap* map = warp == kKeyWarp ? &kmap : &vmap;
+        const uint32_t code_dst = (warp == kKeyWarp ? 0u : static_cast<uint32_t>(kCodeTileBytes)) +
                                   static_cast<uint32_t>(lane * bs * kHeadDim);
-        const uint32_t scale_dst = 2 * kCodeTileBytes + (key_side ? 0u : static_cast<uint32_t>(kTile * 4)) +
-                                   static_cast<uint32_t>(lane * bs * 4);
-        const uint32_t page_bytes = static_cast<uint32_t>(bs) * (kHeadDim + 4);
+        const uint32_t code_bytes = static_cast<uint32_t>(bs * kHeadDim);
+        const uint32_t scale_bytes = static_cast<uint32_t>(bs * 4);
         const int lg_bs = __ffs(static_cast<int>(bs)) - 1;  // block sizes are powers of two
+        const bool gather = t.gather4 != 0;
         uint32_t g = 0, li = 0, q_issued = 0;
         WorkItem nxt = t.items[blockIdx.x];
         for (int item = blockIdx.x; item < count; item += gridDim.x, ++li) {
             const WorkItem it = nxt;
             if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
-            if (key_side) {
+            if (scale_side) {
                 const uint32_t qb = li & 1;
                 if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status)) break;
                 if (lane == 0) {
@@ -415,18 +429,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 bool valid = lane < pages_per_tile && tile0 + (lane << lg_bs) < it.t1;
                 if (valid && (blk < 0 || blk >= a.pool.num_blocks)) {
-                    if (key_side) report_fault(a.status, SDC_FAULT_BLOCK_RANGE);
+                    if (scale_side) report_fault(a.status, SDC_FAULT_BLOCK_RANGE);
                     valid = false;
                 }
                 const uint32_t mask = __ballot_sync(kFullMask, valid);
-                if (lane == 0) mbar_arrive_expect_tx(bar(kvFull + s), __popc(mask) * page_bytes);
-                __syncwarp();
-                if (valid) {
-                    const uint32_t st = stage_base + s * kStageBytes;
-                    const int32_t row = static_cast<int32_t>((blk * a.pool.cbs + code_base) / kHeadDim);
-                    tma_load_2d(st + code_dst, map, 0, row, bar(kvFull + s));
-                    bulk_load(st + scale_dst, scales + blk * a.pool.sbs + scale_base, static_cast<uint32_t>(bs * 4),
-                              bar(kvFull + s));
+                const uint32_t st = stage_base + s * kStageBytes;
+                if (!scale_side) {
+                    if (lane == 0) mbar_arrive_expect_tx(bar(kvFull + s), __popc(mask) * code_bytes);
+                    __syncwarp();
+                    if (valid) {
+                        const int32_t row = static_cast<int32_t>((blk * a.pool.cbs + code_base) / kHeadDim);
+                        tma_load_2d(st + code_dst, map, 0, row, bar(kvFull + s));
+                    }
+                } else if (gather) {
+                    // every group of four pages is copied whole; pages past
+                    // the item read row 0 and are never used
+                    const int32_t srow = valid ? static_cast<int32_t>((blk * a.pool.sbs + scale_base) >> lg_bs) : 0;
+                    if (lane == 0) mbar_arrive_expect_tx(bar(kvFull + s), 2u * pages_per_tile * scale_bytes);
+                    for (int q = 0; q < pages_per_tile; q += 4) {
+                        const int32_t y0 = __shfl_sync(kFullMask, srow, q);
+                        const int32_t y1 = __shfl_sync(kFullMask, srow, q + 1);
+                        const int32_t y2 = __shfl_sync(kFullMask, srow, q + 2);
+                        const int32_t y3 = __shfl_sync(kFullMask, srow, q + 3);
+                        if (lane == 0) {
+                            const uint32_t off = 2 * kCodeTileBytes + q * scale_bytes;
+                            tma_gather4(st + off, &ksmap, y0, y1, y2, y3, bar(kvFull + s));
+                            tma_gather4(st + off + kTile * 4, &vsmap, y0, y1, y2, y3, bar(kvFull + s));
+                        }
+                    }
+                    __syncwarp();
+                } else {
+                    if (lane == 0) mbar_arrive_expect_tx(bar(kvFull + s), __popc(mask) * 2 * scale_bytes);
+                    __syncwarp();
+                    if (valid) {
+                        const int64_t off = blk * a.pool.sbs + scale_base;
+                        const uint32_t dst = st + 2 * kCodeTileBytes + lane * scale_bytes;
+                        bulk_load(dst, a.pool.key_scales + off, scale_bytes, bar(kvFull + s));
+                        bulk_load(dst + kTile * 4, a.pool.value_scales + off, scale_bytes, bar(kvFull + s));
+                    }
                 }
             }
             if (stop) break;
@@ -542,35 +582,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ------------------------------------------------------------ softmax + O epilogue
-        // Warpgroup `grp` takes the tiles with g % 2 == grp.  Cross-warp data
-        // goes through shared memory guarded by the group's xch mbarriers
-        // (one arrival per warp), double-buffered by exchange parity: a buffer
+        // Warpgroup `grp` takes the tiles with g % 2 == grp.  Per tile each
+        // warp reduces its 32 tokens' row maxima (and value-scale maximum)
+        // into shared memory; after the group's exchange (an mbarrier with one
+        // arrival per warp) lanes r < RB of every warp resolve row r's new
+        // running max and rescale factor and hand them to their warp through
+        // the warp's own shared-memory row, read back four rows per load.
+        // Exchange buffers are double-buffered by exchange parity: a buffer
         // is rewritten two exchanges later, by which time every warp of the
         // group has arrived at the exchange in between and so has finished
-        // reading it.  Per-tile rescale data (alpha, changed-row mask, value
-        // factor) are double-buffered by the group's tile parity.
+        // reading it.  Row quantities go two rows at a time through the
+        // packed f32x2 arithmetic of sm_100.
         const int grp = warp >> 2;
         const int qw = warp & 3;            // lane quarter = TMEM lanes [32 qw, 32 qw + 32)
         const int tid = threadIdx.x & 127;  // token row of S^T, head_dim row of O^T
         const uint32_t lane_addr = static_cast<uint32_t>(qw * 32) << 16;
         const uint32_t s_col = grp * LY::kTmemStride;
         const uint32_t o_col = (2 + grp) * LY::kTmemStride;
-        float* red = reinterpret_cast<float*>(smem + LY::kRedOff) + grp * 2 * 4 * (RB + 1);
-        float* alpha_s = reinterpret_cast<float*>(smem + LY::kAlphaOff) + grp * 2 * RB;
-        uint32_t* chg_s = reinterpret_cast<uint32_t*>(smem + LY::kChgOff) + grp * 2;
-        float* vfac_s = reinterpret_cast<float*>(smem + LY::kVfacOff) + grp * 2;
+        constexpr int RS = LY::kRedStride;
+        float* red = reinterpret_cast<float*>(smem + LY::kRedOff) + grp * 2 * 4 * RS;
+        float* wrow = reinterpret_cast<float*>(smem + LY::kWarpOff) + warp * 3 * RB;  // -m[RB], alpha[2][RB]
         float* merge_o = reinterpret_cast<float*>(smem + LY::kMergeOOff);
         float* merge_ml = reinterpret_cast<float*>(smem + LY::kMergeMLOff);
         uint32_t g = 0, li = 0, xc = 0, own = 0, merges = 0;
+        const float2 magic2 = make_float2(kRoundMagic, kRoundMagic);
+        const float2 neg_magic2 = make_float2(-kRoundMagic, -kRoundMagic);
+        const float2 minus_one2 = make_float2(-1.0f, -1.0f);
+        const float2 c254 = make_float2(254.0f, 254.0f);
 
         auto exchange = [&]() -> bool {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(xch + grp * 2 + (xc & 1)));
             return warp_wait(bar(xch + grp * 2 + (xc & 1)), (xc >> 1) & 1, abort_flag, a.status);
         };
-        // O^T tile of this group's k-th tile (the MMA warp alternates buffers
-        // by tile, so the group's k-th use of its O buffer has parity k & 1)
-        auto epilogue = [&](uint32_t k, float (&o_acc)[RB]) -> bool {
+        // Folds O^T of own tile k into the running sums:
+        // o = o * alpha_k + (254 O_hi + O_lo) * vf_k.  The MMA warp alternates
+        // buffers by tile, so the group's k-th use of its O buffer has parity k & 1.
+        auto epilogue = [&](uint32_t k, float vf, float2 (&o_acc)[RB / 2]) -> bool {
             if (!warp_wait(bar(oFull + grp), k & 1, abort_flag, a.status)) return false;
             tc_fence_after();
             uint32_t oreg[N];
@@ -578,14 +626,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(oEmpty + grp));
-            const int par = k & 1;
-            const float vf = vfac_s[par];
-            const uint32_t chg = chg_s[par];
+            const float4* al4 = reinterpret_cast<const float4*>(wrow + RB + (k & 1) * RB);
+            const float2 vf2 = make_float2(vf, vf);
 #pragma unroll
-            for (int r = 0; r < RB; ++r) {
-                const int32_t combined = static_cast<int32_t>(oreg[r]) * 254 + static_cast<int32_t>(oreg[RB + r]);
-                const float prev = ((chg >> r) & 1) ? o_acc[r] * alpha_s[par * RB + r] : o_acc[r];
-                o_acc[r] = fmaf(static_cast<float>(combined), vf, prev);
+            for (int r4 = 0; r4 < RB; r4 += 4) {
+                const float4 al = al4[r4 / 4];
+#pragma unroll
+                for (int j = 0; j < 4; j += 2) {
+                    const int r = r4 + j;
+                    const float c0 = static_cast<float>(static_cast<int32_t>(oreg[r]) * 254 +
+                                                        static_cast<int32_t>(oreg[RB + r]));
+                    const float c1 = static_cast<float>(static_cast<int32_t>(oreg[r + 1]) * 254 +
+                                                        static_cast<int32_t>(oreg[RB + r + 1]));
+                    const float2 a2 = j == 0 ? make_float2(al.x, al.y) : make_float2(al.z, al.w);
+                    o_acc[r / 2] = __ffma2_rn(make_float2(c0, c1), vf2, __fmul2_rn(o_acc[r / 2], a2));
+                }
             }
             return true;
         };
@@ -598,18 +653,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t qb = li & 1;
             if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status)) break;
             const float* qfac = reinterpret_cast<const float*>(smem + LY::kQOff + qb * LY::kQBufBytes + LY::kQCodes);
+            const float qf_lane = lane < RB ? qfac[lane] : 0.0f;
             const int64_t T = it.ctx;
             const int64_t window = a.window;
             const uint32_t row_mask = R >= 32 ? 0xffffffffu : (1u << R) - 1u;
-            float m_lane = -INFINITY;  // lane r holds the running max of row r
-            float l_thr[RB], o_acc[RB];
+            // lane r < RB holds row r's running max of (score * log2 e); the
+            // scores held per token are K-scaled, the query factor applied later
+            float m_lane = -INFINITY;
+            float2 l_thr[RB / 2], o_acc[RB / 2];
 #pragma unroll
-            for (int r = 0; r < RB; ++r) {
-                l_thr[r] = 0.0f;
-                o_acc[r] = 0.0f;
+            for (int r = 0; r < RB / 2; ++r) {
+                l_thr[r] = make_float2(0.0f, 0.0f);
+                o_acc[r] = make_float2(0.0f, 0.0f);
             }
             bool have_prev = false;
             uint32_t prev_own = 0;
+            float vf_prev = 0.0f;
             for (int tile0 = it.t0; tile0 < it.t1; tile0 += kTile, ++g) {
                 if (static_cast<int>(g & 1) != grp) continue;
                 const uint32_t s = g % STAGES;
@@ -625,85 +684,122 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(sEmpty + grp));
 
-                const int64_t tok = tile0 + tid;
-                const bool tvalid = tok < it.t1;
                 const float* sc_ptr =
                     reinterpret_cast<const float*>(smem + LY::kStageOff + s * kStageBytes + 2 * kCodeTileBytes);
                 const float kscale = sc_ptr[tid];
-                const float vscale = tvalid ? sc_ptr[kTile + tid] : 0.0f;
+                float vscale = sc_ptr[kTile + tid];
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kvEmpty + s));
 
-                // a query at window row i sees keys up to T - window + i
-                uint32_t vis_mask = tvalid ? row_mask : 0u;
-                const int64_t past = tok - (T - window);  // > 0: inside the window
-                if (past > 0) {
-                    vis_mask &= past < window ? reinterpret_cast<const uint32_t*>(smem + LY::kCausalOff)[past] : 0u;
+                // Full tiles (every token inside the item and visible to every
+                // row) skip the masking; a query at window row i sees keys up
+                // to T - window + i.
+                const bool full = tile0 + kTile <= it.t1 && tile0 + kTile <= T - window + 1;
+                uint32_t vis_mask = row_mask;
+                if (!full) {
+                    const int64_t tok = tile0 + tid;
+                    if (tok >= it.t1) {
+                        vis_mask = 0u;
+                        vscale = 0.0f;
+                    }
+                    const int64_t past = tok - (T - window);  // > 0: inside the window
+                    if (past > 0) {
+                        vis_mask &= past < window ? reinterpret_cast<const uint32_t*>(smem + LY::kCausalOff)[past] : 0u;
+                    }
                 }
                 float sc[RB];
-                float* red_x = red + (xc & 1) * 4 * (RB + 1);
+                float* red_x = red + (xc & 1) * 4 * RS;
 #pragma unroll
-                for (int r = 0; r < RB; ++r) {
-                    const bool vis = (vis_mask >> r) & 1u;
-                    const int32_t combined = static_cast<int32_t>(sreg[r]) * 254 + static_cast<int32_t>(sreg[RB + r]);
-                    sc[r] = vis ? static_cast<float>(combined) * (qfac[r] * kscale) : -INFINITY;
-                    const float wm = redux_max(sc[r]);
-                    if (lane == 0) red_x[qw * (RB + 1) + r] = wm;
+                for (int r4 = 0; r4 < RB; r4 += 4) {
+                    float wm[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j += 2) {
+                        const int r = r4 + j;
+                        const float c0 = static_cast<float>(static_cast<int32_t>(sreg[r]) * 254 +
+                                                            static_cast<int32_t>(sreg[RB + r]));
+                        const float c1 = static_cast<float>(static_cast<int32_t>(sreg[r + 1]) * 254 +
+                                                            static_cast<int32_t>(sreg[RB + r + 1]));
+                        const float2 s2 = __fmul2_rn(make_float2(c0, c1), make_float2(kscale, kscale));
+                        sc[r] = s2.x;
+                        sc[r + 1] = s2.y;
+                        if (!full) {
+                            if (!((vis_mask >> r) & 1u)) sc[r] = -INFINITY;
+                            if (!((vis_mask >> (r + 1)) & 1u)) sc[r + 1] = -INFINITY;
+                        }
+                        wm[j] = redux_max(sc[r]);
+                        wm[j + 1] = redux_max(sc[r + 1]);
+                    }
+                    if (lane == 0) {
+                        *reinterpret_cast<float4*>(red_x + qw * RS + r4) = make_float4(wm[0], wm[1], wm[2], wm[3]);
+                    }
                 }
                 {
                     const float wv = redux_max(vscale);
-                    if (lane == 0) red_x[qw * (RB + 1) + RB] = wv;
+                    if (lane == 0) red_x[qw * RS + RB] = wv;
                 }
                 if (!exchange()) {
                     ok = false;
                     break;
                 }
                 ++xc;
-                // lane r resolves row r: tile max over the four warps, new
-                // running max, and the rescale factor when the max moved
-                float m_new_lane = -INFINITY, alpha_lane = 1.0f;
+                // lane r resolves row r: tile max over the four warps (times
+                // the query factor, which is >= 0 and so commutes with max),
+                // new running max, and the rescale factor of the old sums
                 if (lane < RB) {
-                    const float tmax = fmaxf(fmaxf(red_x[lane], red_x[(RB + 1) + lane]),
-                                             fmaxf(red_x[2 * (RB + 1) + lane], red_x[3 * (RB + 1) + lane]));
-                    m_new_lane = fmaxf(m_lane, tmax);
-                    if (m_new_lane > m_lane) alpha_lane = (m_lane == -INFINITY) ? 0.0f : fast_exp2(m_lane - m_new_lane);
+                    float tmax = fmaxf(fmaxf(red_x[lane], red_x[RS + lane]),
+                                       fmaxf(red_x[2 * RS + lane], red_x[3 * RS + lane]));
+                    tmax = tmax == -INFINITY ? -INFINITY : tmax * qf_lane;
+                    const float m_new = fmaxf(m_lane, tmax);
+                    float alpha = 1.0f;
+                    if (m_new > m_lane) alpha = m_lane == -INFINITY ? 0.0f : fast_exp2(m_lane - m_new);
+                    m_lane = m_new;
+                    wrow[lane] = -m_new;
+                    wrow[RB + (own & 1) * RB + lane] = alpha;
                 }
-                const uint32_t changed = __ballot_sync(kFullMask, lane < RB && m_new_lane > m_lane);
-                m_lane = m_new_lane;
-                const float vmax = fmaxf(fmaxf(red_x[RB], red_x[(RB + 1) + RB]),
-                                         fmaxf(red_x[2 * (RB + 1) + RB], red_x[3 * (RB + 1) + RB]));
-                const float u_scale = vmax > 0.0f ? 127.0f * vscale / vmax : 0.0f;
+                const float vmax = fmaxf(fmaxf(red_x[RB], red_x[RS + RB]), fmaxf(red_x[2 * RS + RB], red_x[3 * RS + RB]));
+                const float u_scale = vmax > 0.0f ? vscale * __fdividef(127.0f, vmax) : 0.0f;
+                const float2 u2 = make_float2(u_scale, u_scale);
+                const float vf_cur = vmax * (1.0f / (127.0f * 254.0f));
+                __syncwarp();
                 static_assert(RB % 4 == 0, "rows are packed four to a word");
                 uint32_t words[N / 4];  // P^T row: hi bytes in columns [0, RB), lo in [RB, 2 RB)
 #pragma unroll
                 for (int w = 0; w < N / 4; ++w) words[w] = 0u;
+                const float4* nm4 = reinterpret_cast<const float4*>(wrow);
+                const float4* al4 = reinterpret_cast<const float4*>(wrow + RB + (own & 1) * RB);
+                const float4* qf4 = reinterpret_cast<const float4*>(qfac);
 #pragma unroll
                 for (int r4 = 0; r4 < RB; r4 += 4) {
+                    const float4 nm = nm4[r4 / 4];
+                    const float4 al = al4[r4 / 4];
+                    const float4 qf = qf4[r4 / 4];
                     uint32_t th_bits[4], tl_bits[4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                    for (int j = 0; j < 4; j += 2) {
                         const int r = r4 + j;
-                        const float m_r = __shfl_sync(kFullMask, m_new_lane, r);
-                        const float alpha_r = __shfl_sync(kFullMask, alpha_lane, r);
-                        if ((changed >> r) & 1) l_thr[r] *= alpha_r;
-                        const float p = sc[r] == -INFINITY ? 0.0f : fast_exp2(sc[r] - m_r);
-                        l_thr[r] += p;
+                        const float2 nm2 = j == 0 ? make_float2(nm.x, nm.y) : make_float2(nm.z, nm.w);
+                        const float2 al2 = j == 0 ? make_float2(al.x, al.y) : make_float2(al.z, al.w);
+                        const float2 qf2 = j == 0 ? make_float2(qf.x, qf.y) : make_float2(qf.z, qf.w);
+                        float2 e = __ffma2_rn(make_float2(sc[r], sc[r + 1]), qf2, nm2);
+                        if (!full) {
+                            if (sc[r] == -INFINITY) e.x = -INFINITY;
+                            if (sc[r + 1] == -INFINITY) e.y = -INFINITY;
+                        }
+                        const float2 p = make_float2(fast_exp2(e.x), fast_exp2(e.y));
+                        l_thr[r / 2] = __ffma2_rn(l_thr[r / 2], al2, p);
                         // x in [0, 127]: hi = rint(x), lo = rint(254 (x - hi)); adding
                         // 1.5 * 2^23 leaves the rounded integer in the low mantissa bits
-                        const float x = p * u_scale;
-                        const float th = x + kRoundMagic;
-                        const float hi = th - kRoundMagic;
-                        const float tl = fmaf(x - hi, 254.0f, kRoundMagic);
-                        th_bits[j] = __float_as_uint(th);
-                        tl_bits[j] = __float_as_uint(tl);
-                        if (tid == r) alpha_s[(own & 1) * RB + r] = alpha_r;
+                        const float2 x = __fmul2_rn(p, u2);
+                        const float2 th = __fadd2_rn(x, magic2);
+                        const float2 hi = __fadd2_rn(th, neg_magic2);
+                        const float2 tl = __ffma2_rn(__ffma2_rn(hi, minus_one2, x), c254, magic2);
+                        th_bits[j] = __float_as_uint(th.x);
+                        th_bits[j + 1] = __float_as_uint(th.y);
+                        tl_bits[j] = __float_as_uint(tl.x);
+                        tl_bits[j + 1] = __float_as_uint(tl.y);
                     }
                     words[r4 / 4] = pack_low_bytes(th_bits[0], th_bits[1], th_bits[2], th_bits[3]);
                     words[(RB + r4) / 4] = pack_low_bytes(tl_bits[0], tl_bits[1], tl_bits[2], tl_bits[3]);
-                }
-                if (tid == 0) {
-                    chg_s[own & 1] = changed;
-                    vfac_s[own & 1] = vmax / (127.0f * 254.0f);
                 }
                 // P^T row of this token in the MN-major no-swizzle layout: a
                 // 128-byte core matrix holds 16 columns x 8 tokens; 8-token
@@ -721,40 +817,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async();
                 mbar_arrive(bar(pFull + grp * 2 + (own & 1)));
 
-                if (have_prev && !epilogue(prev_own, o_acc)) {
+                if (have_prev && !epilogue(prev_own, vf_prev, o_acc)) {
                     ok = false;
                     break;
                 }
                 have_prev = true;
                 prev_own = own;
+                vf_prev = vf_cur;
                 ++own;
             }
             if (!ok) break;
-            // publish the last tile's rescale data, then its epilogue
-            if (!exchange()) break;
-            ++xc;
-            if (have_prev && !epilogue(prev_own, o_acc)) break;
+            if (have_prev && !epilogue(prev_own, vf_prev, o_acc)) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(qEmpty + qb));
             // this group's row sums over all its tokens
-            float* red_x = red + (xc & 1) * 4 * (RB + 1);
+            float* red_x = red + (xc & 1) * 4 * RS;
 #pragma unroll
             for (int r = 0; r < RB; ++r) {
-                const float ws = warp_sum(l_thr[r]);
-                if (lane == 0) red_x[qw * (RB + 1) + r] = ws;
+                const float ws = warp_sum((r & 1) ? l_thr[r / 2].y : l_thr[r / 2].x);
+                if (lane == 0) red_x[qw * RS + r] = ws;
             }
             if (!exchange()) break;
             ++xc;
             float l_lane = 0.0f;
             if (lane < RB) {
-                l_lane = red_x[lane] + red_x[(RB + 1) + lane] + red_x[2 * (RB + 1) + lane] +
-                         red_x[3 * (RB + 1) + lane];
+                l_lane = red_x[lane] + red_x[RS + lane] + red_x[2 * RS + lane] + red_x[3 * RS + lane];
             }
             // merge the two groups' states: group 1 hands its state to group 0
             if (grp == 1) {
                 if (!warp_wait(bar(mergeEmpty), (merges & 1) ^ 1, abort_flag, a.status)) break;
 #pragma unroll
-                for (int r = 0; r < RB; ++r) merge_o[tid * RB + r] = o_acc[r];
+                for (int r = 0; r < RB; r += 2) *reinterpret_cast<float2*>(merge_o + tid * RB + r) = o_acc[r / 2];
                 if (qw == 0 && lane < RB) {
                     merge_ml[2 * lane + 0] = m_lane;
                     merge_ml[2 * lane + 1] = l_lane;
@@ -782,7 +875,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int r = 0; r < RB; ++r) {
                     const float e0 = __shfl_sync(kFullMask, e0_lane, r);
                     const float e1 = __shfl_sync(kFullMask, e1_lane, r);
-                    if (r < R) part_o[r * kHeadDim + tid] = o_acc[r] * e0 + merge_o[tid * RB + r] * e1;
+                    const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
+                    if (r < R) part_o[r * kHeadDim + tid] = o0 * e0 + merge_o[tid * RB + r] * e1;
                 }
                 if (qw == 0 && lane < R) {
                     part_ml[2 * lane + 0] = m_tot;
@@ -959,6 +1053,26 @@ bool make_page_map(CUtensorMap* map, const int8_t* codes, const Pool& p) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over a scale array as rows of block_size floats (one page's
+// scales); one box = one row, read four rows at a time by tile::gather4.
+// Needs every page's scales to start on a row boundary.
+bool make_scale_map(CUtensorMap* map, const float* scales, const Pool& p) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return false;
+    const int64_t bs = p.block_size;
+    if (p.sbs % bs || p.sls % bs || p.shs % bs) return false;
+    const int64_t last = (p.num_blocks - 1) * p.sbs + (p.num_layers - 1) * p.sls + (p.num_heads - 1) * p.shs;
+    const uint64_t rows = static_cast<uint64_t>(last / bs + 1);
+    if (rows > (uint64_t(1) << 31)) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(bs), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(bs * 4)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(bs), 1};
+    cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(scales), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_64B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Row buckets with a compiled kernel; rows are padded up to the bucket.
 int bucket_for(int64_t rows) {
     if (rows <= 0) return 0;
@@ -982,8 +1096,8 @@ int num_sms() {
 }
 
 template <int RB>
-sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap, int32_t* first,
-                           cudaStream_t st) {
+sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                           const CUtensorMap& ksmap, const CUtensorMap& vsmap, int32_t* first, cudaStream_t st) {
     using LY = Rows<RB>;
     const int64_t query_warps = t.a.batch * t.a.kv_heads * RB;
     prep_kernel<RB><<<static_cast<unsigned>(1 + (query_warps + 31) / 32), 1024, 0, st>>>(t, first);
@@ -998,7 +1112,7 @@ sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUten
     }
     const int64_t max_items = t.a.batch * t.a.kv_heads * t.a.max_chunks;
     const int64_t grid = std::min<int64_t>(num_sms(), max_items);
-    kernel<<<static_cast<unsigned>(grid), kThreads, LY::kDynamicSmem, st>>>(kmap, vmap, t);
+    kernel<<<static_cast<unsigned>(grid), kThreads, LY::kDynamicSmem, st>>>(kmap, vmap, ksmap, vsmap, t);
     return launch_status();
 }
 
@@ -1045,17 +1159,24 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
     base += up(a.batch * 4);
     t.qimg = reinterpret_cast<unsigned char*>(base);
     t.rows = static_cast<int32_t>(a.rows);
-    CUtensorMap kmap, vmap;
+    CUtensorMap kmap, vmap, ksmap, vsmap;
     if (!make_page_map(&kmap, a.pool.keys, a.pool) || !make_page_map(&vmap, a.pool.values, a.pool)) {
         return SDC_STATUS_CUDA_ERROR;
     }
+    // gathers need whole groups of four pages per tile and row-aligned scales
+    t.gather4 = (kTile / a.pool.block_size) % 4 == 0 && make_scale_map(&ksmap, a.pool.key_scales, a.pool) &&
+                make_scale_map(&vsmap, a.pool.value_scales, a.pool);
+    if (!t.gather4) {
+        ksmap = kmap;  // unused
+        vsmap = vmap;
+    }
     sdc_status_t rc;
     switch (bucket_for(a.rows)) {
-        case 8: rc = launch_bucket<8>(t, kmap, vmap, first, st); break;
-        case 16: rc = launch_bucket<16>(t, kmap, vmap, first, st); break;
-        case 20: rc = launch_bucket<20>(t, kmap, vmap, first, st); break;
-        case 24: rc = launch_bucket<24>(t, kmap, vmap, first, st); break;
-        case 32: rc = launch_bucket<32>(t, kmap, vmap, first, st); break;
+        case 8: rc = launch_bucket<8>(t, kmap, vmap, ksmap, vsmap, first, st); break;
+        case 16: rc = launch_bucket<16>(t, kmap, vmap, ksmap, vsmap, first, st); break;
+        case 20: rc = launch_bucket<20>(t, kmap, vmap, ksmap, vsmap, first, st); break;
+        case 24: rc = launch_bucket<24>(t, kmap, vmap, ksmap, vsmap, first, st); break;
+        case 32: rc = launch_bucket<32>(t, kmap, vmap, ksmap, vsmap, first, st); break;
         default: return SDC_STATUS_UNSUPPORTED;
     }
     if (rc != SDC_STATUS_OK) return rc;
