@@ -56,7 +56,8 @@ typedef enum sdc_status {
     SDC_STATUS_UNSUPPORTED = 12,
     SDC_STATUS_MISALIGNED = 13,
     SDC_STATUS_DEVICE_FAULT = 14,
-    SDC_STATUS_INVALID_ARGUMENT = 15
+    SDC_STATUS_INVALID_ARGUMENT = 15,
+    SDC_STATUS_SCRATCH_EXCEEDED = 16
 } sdc_status_t;
 
 /* Bits a kernel ORs into the device status word. */
@@ -210,6 +211,30 @@ SDC_API sdc_status_t sdc_paged_verify_attention(
  * (src/specdecode/kv_cache.py:349-380) and the CPU reconstruct of
  * HuggingFacePagedCacheMirror.materialize_legacy_cache (src/specdecode/hf_paged_cache.py:247-313).
  */
+/* Bytes of the library-owned scratch of sdc_paged_verify_attention_no_alloc. */
+#define SDC_NO_ALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+
+/*
+ * sdc_paged_verify_attention without a caller workspace, for callers that may
+ * not allocate device memory (a serving loop whose memory another allocator
+ * has reserved up front, a plugin host that hands over only its input and
+ * output buffers, a callback that must not synchronize the device as
+ * cudaMalloc / cudaFree can).  Same arguments, results and errors as
+ * sdc_paged_verify_attention minus workspace / workspace_bytes; the workspace
+ * is a SDC_NO_ALLOC_SCRATCH_BYTES device array that each GPU loading the
+ * library holds until exit.  Shapes needing more (see
+ * sdc_paged_attention_workspace_size) return SDC_STATUS_SCRATCH_EXCEEDED
+ * before any launch.  Calls on one device share the array: calls that overlap
+ * on the GPU race, so keep them on one stream.  The first call on a device
+ * looks up the array's address with that device current; make it before any
+ * stream capture.  No counterpart in the reference.
+ */
+SDC_API sdc_status_t sdc_paged_verify_attention_no_alloc(
+    const sdc_page_pool_t* pool, int64_t layer, const void* query, int query_dtype,
+    int64_t batch, int64_t num_query_heads, int64_t window, const int32_t* block_tables,
+    int64_t table_stride, const int32_t* context_lens, int64_t max_context_len, void* out,
+    int32_t* device_status, uintptr_t stream);
+
 SDC_API sdc_status_t sdc_gather_dequantize(
     const sdc_page_pool_t* pool, int64_t layer_begin, int64_t num_layers,
     const int64_t* slot_mapping, int64_t num_tokens, void* out_keys, void* out_values,

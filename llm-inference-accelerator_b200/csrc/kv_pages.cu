@@ -457,6 +457,7 @@ SDC_API const char* sdc_status_string(sdc_status_t status) {
         case SDC_STATUS_MISALIGNED: return "buffer or stride is not 16-byte aligned";
         case SDC_STATUS_DEVICE_FAULT: return "a kernel reported a fault in the device status word";
         case SDC_STATUS_INVALID_ARGUMENT: return "invalid argument";
+        case SDC_STATUS_SCRATCH_EXCEEDED: return "workspace larger than the library's fixed scratch";
         default: return "unknown status";
     }
 }

@@ -31,6 +31,7 @@ STATUS_UNSUPPORTED = 12
 STATUS_MISALIGNED = 13
 STATUS_DEVICE_FAULT = 14
 STATUS_INVALID_ARGUMENT = 15
+STATUS_SCRATCH_EXCEEDED = 16
 
 FAULT_NONFINITE_VALUE = 0x01
 FAULT_INVALID_SCALE = 0x02
@@ -66,6 +67,7 @@ EXPORTED_SYMBOLS = (
     "sdc_paged_attention_workspace_size",
     "sdc_paged_verify_attention",
     "sdc_gather_dequantize",
+    "sdc_paged_verify_attention_no_alloc",
 )
 
 
@@ -180,6 +182,9 @@ class CudaLibrary:
             ctypes.POINTER(PagePool), i64, vp, ctypes.c_int, i64, i64, i64, vp, i64, vp, i64, vp, vp,
             ctypes.c_size_t, vp, u]
         h.sdc_paged_verify_attention.restype = ctypes.c_int
+        h.sdc_paged_verify_attention_no_alloc.argtypes = [
+            ctypes.POINTER(PagePool), i64, vp, ctypes.c_int, i64, i64, i64, vp, i64, vp, i64, vp, vp, u]
+        h.sdc_paged_verify_attention_no_alloc.restype = ctypes.c_int
         h.sdc_gather_dequantize.argtypes = [
             ctypes.POINTER(PagePool), i64, i64, vp, i64, vp, vp, ctypes.c_int, i64, i64, i64, vp, u]
         h.sdc_gather_dequantize.restype = ctypes.c_int
