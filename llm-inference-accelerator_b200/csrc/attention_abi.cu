@@ -34,7 +34,7 @@ sdc_status_t make_plan(int64_t batch, int64_t hq, int64_t hkv, int64_t d, int64_
     p->rows = (hq / hkv) * window;
     if (!simt_supports(d, p->rows)) return SDC_STATUS_UNSUPPORTED;
     p->tensor_cores = tc::shape_supported(d, p->rows);
-    p->chunk = p->tensor_cores ? tc::chunk_for(batch, hkv, max_ctx) : kSimtChunk;
+    p->chunk = p->tensor_cores ? tc::chunk_for(batch, hkv, max_ctx, p->rows) : kSimtChunk;
     p->max_chunks = ceil_div(max_ctx, p->chunk);
     if (!combine_fits(p->max_chunks, p->rows)) return SDC_STATUS_UNSUPPORTED;
     const double items = static_cast<double>(batch) * hkv * p->max_chunks;

@@ -40,12 +40,12 @@ sdc_status_t launch_attention_combine(const AttnArgs& a, cudaStream_t stream);
 bool combine_fits(int64_t max_chunks, int64_t rows);
 
 namespace tc {
-// Shapes the tensor-core item kernel serves: head_dim 128 and at most 40
-// query rows per KV head.
+// Shapes the tensor-core item kernel serves: head_dim 128 and at most 64
+// query rows per KV head (more than 32 are split over two items).
 bool shape_supported(int64_t head_dim, int64_t rows);
 // Pool layouts it can read with TMA (page rows of 128 bytes, aligned scales).
 bool supports(const AttnArgs& a);
-int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len);
+int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len, int64_t rows);
 size_t extra_workspace(int64_t batch, int64_t kv_heads, int64_t max_chunks, int64_t rows);
 sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t stream);
 }  // namespace tc

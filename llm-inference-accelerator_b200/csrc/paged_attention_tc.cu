@@ -57,6 +57,9 @@ constexpr int kValueWarp = 10;  // value codes of every page
 constexpr int kScaleWarp = 11;  // key and value scales of every page, query images
 constexpr int kThreads = 12 * 32;
 constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
+// A KV head's query rows (GQA group x window) beyond 32 are split over up
+// to kMaxSplits items per chunk, each serving at most 32 rows.
+constexpr int kMaxSplits = 2;
 
 template <int RB>
 struct Rows {
@@ -83,8 +86,8 @@ struct Rows {
     static constexpr int kBarOff = ((kMergeMLOff + RB * 8 + 7) / 8) * 8;
     static constexpr int kNumBars = 2 * kStages + 2 * 7 + 2 + 2 * kGroups + 2;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-    static constexpr int kCausalOff = kMiscOff + 16;  // [32] row masks of the causal window
-    static constexpr int kTotal = kCausalOff + 32 * 4;
+    static constexpr int kCausalOff = kMiscOff + 16;  // [split][32] row masks of the causal window
+    static constexpr int kTotal = kCausalOff + kMaxSplits * 32 * 4;
     static constexpr int kDynamicSmem = kTotal + 1024;
     static_assert(kDynamicSmem <= 232448, "shared memory per block");
     static_assert(RB <= 32, "row masks are 32 bits");
@@ -97,9 +100,10 @@ constexpr int64_t query_image_stride(int rb) {
 }
 
 // One unit of work: tokens [t0, t1) of sequence b (context length ctx) for
-// KV head h; chunk = t0 / chunk size, the partial's slot.
+// query-row split `split` of KV head h; chunk = t0 / chunk size, the
+// partial's slot.
 struct __align__(32) WorkItem {
-    int32_t b, h, t0, t1, ctx, chunk, pad0, pad1;
+    int32_t b, h, t0, t1, ctx, chunk, split, pad;
 };
 
 struct TcArgs {
@@ -110,7 +114,9 @@ struct TcArgs {
     // in the score MMA's B layout, then the row factors (written by the
     // planning launch)
     unsigned char* qimg;
-    int32_t rows;        // query rows per KV head (<= RB)
+    int32_t rows;        // query rows per split (<= RB); the last split may hold fewer
+    int32_t splits;      // row splits per KV head
+    int32_t total_rows;  // query rows per KV head (group x window)
     int32_t gather4;     // scales fetched four pages per copy through the scale maps
 };
 
@@ -347,12 +353,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (threadIdx.x < 32) {
-        // causal[j]: the rows a key j positions past the last fully visible
-        // one stays visible to (row r = group row * window + i sees i >= j)
+    if (threadIdx.x < kMaxSplits * 32) {
+        // causal[split][j]: the split's rows that a key j positions past the
+        // last fully visible one stays visible to (query row q = group row *
+        // window + i sees i >= j)
+        const int sp = threadIdx.x >> 5, j = threadIdx.x & 31;
         uint32_t m = 0;
         for (int r = 0; r < t.rows; ++r) {
-            if (r % a.window >= static_cast<int>(threadIdx.x)) m |= 1u << r;
+            const int q = sp * t.rows + r;
+            if (q < t.total_rows && q % a.window >= j) m |= 1u << r;
         }
         reinterpret_cast<uint32_t*>(smem + LY::kCausalOff)[threadIdx.x] = m;
     }
@@ -371,7 +380,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stage_base = smem_u32(smem + LY::kStageOff);
     const uint32_t q_base = smem_u32(smem + LY::kQOff);
     const uint32_t p_base = smem_u32(smem + LY::kPOff);
-    const int R = t.rows;
     const int64_t bs = a.pool.block_size;
     const int pages_per_tile = static_cast<int>(kTile / bs);
 
@@ -399,9 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t qb = li & 1;
                 if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status)) break;
                 if (lane == 0) {
-                    const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
+                    const int64_t image = (static_cast<int64_t>(it.b) * a.kv_heads + it.h) * t.splits + it.split;
                     mbar_arrive_expect_tx(bar(qFull + qb), LY::kQCopyBytes);
-                    bulk_load(q_base + qb * LY::kQBufBytes, t.qimg + bh * LY::kQStride, LY::kQCopyBytes,
+                    bulk_load(q_base + qb * LY::kQBufBytes, t.qimg + image * LY::kQStride, LY::kQCopyBytes,
                               bar(qFull + qb));
                 }
                 __syncwarp();
@@ -656,7 +664,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float qf_lane = lane < RB ? qfac[lane] : 0.0f;
             const int64_t T = it.ctx;
             const int64_t window = a.window;
+            const int row0 = it.split * t.rows;               // first query row of this item
+            const int R = min(t.rows, t.total_rows - row0);   // its rows
             const uint32_t row_mask = R >= 32 ? 0xffffffffu : (1u << R) - 1u;
+            const uint32_t* causal = reinterpret_cast<const uint32_t*>(smem + LY::kCausalOff) + it.split * 32;
             // lane r < RB holds row r's running max of (score * log2 e); the
             // scores held per token are K-scaled, the query factor applied later
             float m_lane = -INFINITY;
@@ -704,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const int64_t past = tok - (T - window);  // > 0: inside the window
                     if (past > 0) {
-                        vis_mask &= past < window ? reinterpret_cast<const uint32_t*>(smem + LY::kCausalOff)[past] : 0u;
+                        vis_mask &= past < window ? causal[past] : 0u;
                     }
                 }
                 float sc[RB];
@@ -869,8 +880,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
                 const int64_t chunk = it.chunk;
-                float* part_o = a.part_o + (bh * a.max_chunks + chunk) * R * kHeadDim;
-                float* part_ml = a.part_ml + (bh * a.max_chunks + chunk) * R * 2;
+                float* part_o = a.part_o + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * kHeadDim;
+                float* part_ml = a.part_ml + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * 2;
 #pragma unroll
                 for (int r = 0; r < RB; ++r) {
                     const float e0 = __shfl_sync(kFullMask, e0_lane, r);
@@ -914,16 +925,18 @@ __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
     if (blockIdx.x > 0) {
         const int lane = threadIdx.x & 31;
         const int64_t w = static_cast<int64_t>(blockIdx.x - 1) * 32 + (threadIdx.x >> 5);
-        const int64_t bh = w / RB;
-        const int r = static_cast<int>(w - bh * RB);
-        if (bh >= a.batch * a.kv_heads) return;
+        const int64_t image = w / RB;  // (sequence, KV head, split)
+        const int r = static_cast<int>(w - image * RB);
+        if (image >= a.batch * a.kv_heads * t.splits) return;
+        const int64_t bh = image / t.splits;
+        const int64_t row = (image - bh * t.splits) * t.rows + r;  // query row within the KV head
         const int64_t b = bh / a.kv_heads;
         const int64_t h = bh - b * a.kv_heads;
-        unsigned char* img = t.qimg + bh * LY::kQStride;
+        unsigned char* img = t.qimg + image * LY::kQStride;
         const int d = lane * 4;
         float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (r < t.rows) {
-            const int64_t e = ((b * a.query_heads + h * a.group) * a.window + r) * kHeadDim + d;
+        if (r < t.rows && row < t.total_rows) {
+            const int64_t e = ((b * a.query_heads + h * a.group) * a.window + row) * kHeadDim + d;
             if (a.query_dtype == SDC_DTYPE_BF16) {
                 const uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.query) + e));
                 x[0] = __uint_as_float(v.x << 16);
@@ -984,7 +997,7 @@ __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
             const bool valid =
                 T >= a.window && T <= a.table_stride * a.pool.block_size && T <= a.max_chunks * a.chunk;
             if (!valid) report_fault(a.status, SDC_FAULT_CONTEXT_RANGE);
-            n = valid ? static_cast<int32_t>(((T + a.chunk - 1) / a.chunk) * a.kv_heads) : 0;
+            n = valid ? static_cast<int32_t>(((T + a.chunk - 1) / a.chunk) * a.kv_heads * t.splits) : 0;
         }
         int32_t off, total;
         Scan(temp).ExclusiveSum(n, off, total);
@@ -1000,17 +1013,22 @@ __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
         if (!valid) continue;
         const int64_t chunks = (T + a.chunk - 1) / a.chunk;
         WorkItem* out = const_cast<WorkItem*>(t.items) + first[b];
+        // the splits of one chunk are adjacent, so they run on neighbouring
+        // SMs at about the same time and the second reads its pages from L2
         for (int64_t c = 0; c < chunks; ++c) {
             for (int64_t h = 0; h < a.kv_heads; ++h) {
-                WorkItem w;
-                w.b = static_cast<int32_t>(b);
-                w.h = static_cast<int32_t>(h);
-                w.t0 = static_cast<int32_t>(c * a.chunk);
-                w.t1 = static_cast<int32_t>(min(T, (c + 1) * a.chunk));
-                w.ctx = static_cast<int32_t>(T);
-                w.chunk = static_cast<int32_t>(c);
-                w.pad0 = w.pad1 = 0;
-                out[c * a.kv_heads + h] = w;
+                for (int sp = 0; sp < t.splits; ++sp) {
+                    WorkItem w;
+                    w.b = static_cast<int32_t>(b);
+                    w.h = static_cast<int32_t>(h);
+                    w.t0 = static_cast<int32_t>(c * a.chunk);
+                    w.t1 = static_cast<int32_t>(min(T, (c + 1) * a.chunk));
+                    w.ctx = static_cast<int32_t>(T);
+                    w.chunk = static_cast<int32_t>(c);
+                    w.split = sp;
+                    w.pad = 0;
+                    out[(c * a.kv_heads + h) * t.splits + sp] = w;
+                }
             }
         }
     }
@@ -1084,6 +1102,13 @@ int bucket_for(int64_t rows) {
     return 0;
 }
 
+// Query-row splits of a KV head's rows, and rows per split.
+int64_t splits_for(int64_t rows) { return (rows + 31) / 32; }
+int64_t split_rows(int64_t rows) {
+    const int64_t sp = splits_for(rows);
+    return sp > 0 ? (rows + sp - 1) / sp : 0;
+}
+
 int num_sms() {
     static int sms = 0;
     if (sms == 0) {
@@ -1099,7 +1124,7 @@ template <int RB>
 sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap,
                            const CUtensorMap& ksmap, const CUtensorMap& vsmap, int32_t* first, cudaStream_t st) {
     using LY = Rows<RB>;
-    const int64_t query_warps = t.a.batch * t.a.kv_heads * RB;
+    const int64_t query_warps = t.a.batch * t.a.kv_heads * t.splits * RB;
     prep_kernel<RB><<<static_cast<unsigned>(1 + (query_warps + 31) / 32), 1024, 0, st>>>(t, first);
     auto kernel = attn_tc_kernel<RB>;
     static bool configured = false;
@@ -1110,7 +1135,7 @@ sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUten
         }
         configured = true;
     }
-    const int64_t max_items = t.a.batch * t.a.kv_heads * t.a.max_chunks;
+    const int64_t max_items = t.a.batch * t.a.kv_heads * t.a.max_chunks * t.splits;
     const int64_t grid = std::min<int64_t>(num_sms(), max_items);
     kernel<<<static_cast<unsigned>(grid), kThreads, LY::kDynamicSmem, st>>>(kmap, vmap, ksmap, vsmap, t);
     return launch_status();
@@ -1118,7 +1143,9 @@ sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUten
 
 }  // namespace
 
-bool shape_supported(int64_t head_dim, int64_t rows) { return head_dim == kHeadDim && bucket_for(rows) != 0; }
+bool shape_supported(int64_t head_dim, int64_t rows) {
+    return head_dim == kHeadDim && rows >= 1 && splits_for(rows) <= kMaxSplits && bucket_for(split_rows(rows)) != 0;
+}
 
 bool supports(const AttnArgs& a) {
     const Pool& p = a.pool;
@@ -1129,11 +1156,11 @@ bool supports(const AttnArgs& a) {
            (reinterpret_cast<uintptr_t>(p.value_scales) & 15) == 0 && encode_fn() != nullptr;
 }
 
-int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len) {
+int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len, int64_t rows) {
     // about four items per SM when every sequence is at the maximum length;
     // a multiple of the tile
     const int64_t slots = static_cast<int64_t>(num_sms()) * 4;
-    int64_t c = (batch * kv_heads * max_context_len + slots - 1) / slots;
+    int64_t c = (batch * kv_heads * splits_for(rows) * max_context_len + slots - 1) / slots;
     c = (c + kTile - 1) / kTile * kTile;
     if (c < 512) c = 512;
     if (c > 16384) c = 16384;
@@ -1142,8 +1169,9 @@ int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len) {
 
 size_t extra_workspace(int64_t batch, int64_t kv_heads, int64_t max_chunks, int64_t rows) {
     auto up = [](int64_t v) { return static_cast<size_t>((v + 255) / 256 * 256); };
-    return up(batch * kv_heads * max_chunks * static_cast<int64_t>(sizeof(WorkItem))) + up(16) + up(batch * 4) +
-           up(batch * kv_heads * query_image_stride(bucket_for(rows)));
+    const int64_t sp = splits_for(rows);
+    return up(batch * kv_heads * max_chunks * sp * static_cast<int64_t>(sizeof(WorkItem))) + up(16) +
+           up(batch * 4) + up(batch * kv_heads * sp * query_image_stride(bucket_for(split_rows(rows))));
 }
 
 sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
@@ -1151,14 +1179,16 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
     char* base = static_cast<char*>(extra);
     TcArgs t;
     t.a = a;
+    t.splits = static_cast<int32_t>(splits_for(a.rows));
+    t.rows = static_cast<int32_t>(split_rows(a.rows));
+    t.total_rows = static_cast<int32_t>(a.rows);
     t.items = reinterpret_cast<const WorkItem*>(base);
-    base += up(a.batch * a.kv_heads * a.max_chunks * static_cast<int64_t>(sizeof(WorkItem)));
+    base += up(a.batch * a.kv_heads * a.max_chunks * t.splits * static_cast<int64_t>(sizeof(WorkItem)));
     t.item_count = reinterpret_cast<const int32_t*>(base);
     base += up(16);
     int32_t* first = reinterpret_cast<int32_t*>(base);
     base += up(a.batch * 4);
     t.qimg = reinterpret_cast<unsigned char*>(base);
-    t.rows = static_cast<int32_t>(a.rows);
     CUtensorMap kmap, vmap, ksmap, vsmap;
     if (!make_page_map(&kmap, a.pool.keys, a.pool) || !make_page_map(&vmap, a.pool.values, a.pool)) {
         return SDC_STATUS_CUDA_ERROR;
@@ -1171,7 +1201,7 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
         vsmap = vmap;
     }
     sdc_status_t rc;
-    switch (bucket_for(a.rows)) {
+    switch (bucket_for(t.rows)) {
         case 8: rc = launch_bucket<8>(t, kmap, vmap, ksmap, vsmap, first, st); break;
         case 16: rc = launch_bucket<16>(t, kmap, vmap, ksmap, vsmap, first, st); break;
         case 20: rc = launch_bucket<20>(t, kmap, vmap, ksmap, vsmap, first, st); break;

@@ -86,6 +86,9 @@ CASES = [
     (64, 8, 128, 5, 16, 1, 0, [5, 129, 2048]),
     (4, 1, 256, 8, 32, 1, 0, [8, 40, 600]),
     (16, 4, 64, 5, 16, 3, 2, [100, 1537]),
+    # more than 32 query rows per KV head: split over two items per chunk
+    (64, 8, 128, 8, 16, 1, 0, [8, 300, 4100]),
+    (24, 8, 128, 11, 16, 2, 1, [11, 777, 2500]),
 ]
 
 
@@ -179,6 +182,45 @@ def test_full_verify_shape_subset_and_properties(device):
     tt2 = perm[tt.long().clamp(min=0)].to(torch.int32).masked_fill(tt < 0, -1)
     out2 = _attention(cache)(qt, tt2, lt, int(lens.max()), 0).float()
     assert torch.equal(out, out2)
+
+
+def test_long_context_70b_shape(device):
+    """Llama-3.1-70B long-context verify (8 sequences x 131072 tokens, 64
+    query / 8 KV heads, window 5: 40 query rows per KV head, served as two
+    20-row splits) against the unfused reference computation run with torch
+    on the device, every sequence."""
+    import torch
+
+    from oracle.workloads import VERIFY_70B, verify_inputs
+
+    shape = VERIFY_70B
+    lens, tables, nb, q = verify_inputs(shape, seed=77)
+    gen = torch.Generator(device=device).manual_seed(70)
+    cache = make_cache(device, 1, shape.kv_heads, shape.head_dim, shape.block_size, nb)
+    cache.create_sequence("fill")
+    step = 1 << 16
+    for start in range(0, nb * shape.block_size, step):
+        n = min(step, nb * shape.block_size - start)
+        k = torch.randn((n, 1, shape.kv_heads, shape.head_dim), generator=gen, device=device, dtype=torch.bfloat16)
+        v = torch.randn((n, 1, shape.kv_heads, shape.head_dim), generator=gen, device=device, dtype=torch.bfloat16)
+        cache.append_tensor("fill", k, v)
+    qt = torch.from_numpy(q).to(torch.bfloat16).to(device)
+    tt = tables_tensor(tables, device)
+    lt = torch.tensor(lens, dtype=torch.int32, device=device)
+    out = _attention(cache)(qt, tt, lt, int(lens.max()), 0).float()
+    torch.cuda.synchronize()
+    assert cache.status_bits() == 0
+    keys_v, vals_v = cache.keys_view[:, :, 0], cache.values_view[:, :, 0]
+    ks_v, vs_v = cache.key_scales_view[:, :, 0], cache.value_scales_view[:, :, 0]
+    for b in range(shape.batch):
+        T = int(lens[b])
+        t = torch.arange(T, device=device)
+        blk = torch.from_numpy(tables[b]).to(device)[t // shape.block_size]
+        off = t % shape.block_size
+        ref = attention_reference_torch_flat(qt[b], keys_v[blk, off], vals_v[blk, off], ks_v[blk, off],
+                                             vs_v[blk, off]).float()
+        err = (out[b] - ref).abs()
+        assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS, (b, float(err.max()))
 
 
 def test_faults_are_reported_not_trapped(device):
