@@ -41,6 +41,7 @@ METRIC = "paged INT8 verify-attn HBM GB/s (% of peak) at 1/2/4/8 B200; append to
 VERIFY = dict(batch=32, query_heads=32, kv_heads=8, head_dim=128, window=5, block_size=16,
               min_context=1024, max_context=8192)
 APPEND = dict(layers=32, kv_heads=8, head_dim=128, sequences=256, window=5, block_size=16, num_blocks=65536)
+LONG = dict(batch=8, query_heads=64, kv_heads=8, head_dim=128, window=5, block_size=16, context=131072)
 FLUSH_BYTES = 256 << 20
 
 
@@ -53,6 +54,7 @@ def parse_args(argv=None):
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--skip-append", action="store_true", help="measure only the verify attention")
     p.add_argument("--skip-cpu-baseline", action="store_true")
+    p.add_argument("--skip-long", action="store_true", help="skip the 70B long-context (KV-head parallel) workload")
     p.add_argument("--profile", action="store_true",
                    help="verify attention only: no clock sampling, sustained load, host-buffer pass, append "
                         "workload or CPU baseline (a short, repeatable run for ncu)")
@@ -395,6 +397,81 @@ def run_append(seed: int, device, steps: int, warmup: int, world: int, flush):
 # CPU baseline (the reference's CPU path, bounded sample)
 # ---------------------------------------------------------------------------
 
+def run_long_context(seed: int, rank: int, world: int, device, steps: int, warmup: int):
+    """Llama-3.1-70B long-context verify, one layer: 8 sequences x 131072
+    tokens, 64 query / 8 KV heads, window 5.  KV heads are split over the
+    ranks (tensor parallel); each rank holds its heads' pages of every
+    sequence and the outputs are all-gathered over NCCL.  Strong scaling:
+    the total work is fixed."""
+    import numpy as np
+    import torch
+
+    from specdecode_b200.cuda_kv_cache import PagedVerifyAttention, attention_bytes
+    from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
+    from specdecode_b200.sharding import TensorParallelVerifyAttention, head_shard, shard_query
+
+    c = LONG
+    shard = head_shard(rank, world, c["kv_heads"], c["query_heads"])
+    B, T, bs, D, kw = c["batch"], c["context"], c["block_size"], c["head_dim"], c["window"]
+    per_seq = T // bs
+    nb = B * per_seq
+    cache = PagedKVCache(KVCacheConfig(1, shard.kv_per_rank, D, block_size=bs, num_blocks=nb), device=device,
+                         max_sequences=1, check_status=False)
+    gen = torch.Generator(device=device).manual_seed(seed + 17 * rank)
+    cache.create_sequence("fill")
+    step = 1 << 16
+    for start in range(0, nb * bs, step):
+        n = min(step, nb * bs - start)
+        k = torch.randn((n, 1, shard.kv_per_rank, D), generator=gen, device=device, dtype=torch.bfloat16)
+        v = torch.randn((n, 1, shard.kv_per_rank, D), generator=gen, device=device, dtype=torch.bfloat16)
+        cache.append_tensor("fill", k, v)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(seed)  # the same tables and queries on every rank
+    tables = torch.from_numpy(rng.permutation(nb).astype(np.int32).reshape(B, per_seq)).to(device)
+    lens = torch.full((B,), T, dtype=torch.int32, device=device)
+    query = torch.from_numpy(rng.standard_normal((B, c["query_heads"], kw, D), dtype=np.float32)).to(
+        torch.bfloat16).to(device)
+    attention = PagedVerifyAttention.for_cache(cache)
+    tp = TensorParallelVerifyAttention(attention, shard)
+    q_local = shard_query(query, shard).contiguous()
+    out_local = torch.empty_like(q_local)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        barrier(world)
+        torch.cuda.synchronize()
+        for i in range(steps):
+            starts[i].record(stream)
+            fn()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps, world)
+
+    local_ms = timed(lambda: attention(q_local, tables, lens, T, 0, out=out_local))
+    full_ms = timed(lambda: tp(query, tables, lens, T, 0))
+    if cache.status_bits():
+        raise RuntimeError(f"device fault bits 0x{cache.status_bits():x} in the long-context benchmark")
+    per_rank = attention_bytes([T] * B, shard.q_per_rank, shard.kv_per_rank, D, kw, bs)
+    total = sum_over_ranks(per_rank, world)
+    return {
+        "config": "70B long-context verify, one layer: B8 x 131072 tokens, Hq64 Hkv8 D128 window5 bs16, "
+                  "randomly permuted blocks",
+        "parallelism": f"KV-head tensor-parallel x{world}" + (" + NCCL all-gather of outputs" if world > 1 else ""),
+        "scaling": "strong",
+        "gbs": total / (local_ms / 1e3) / 1e9,
+        "ms_per_step": local_ms,
+        "gbs_with_allgather": total / (full_ms / 1e3) / 1e9,
+        "ms_per_step_with_allgather": full_ms,
+        "allgather_bytes": B * c["query_heads"] * kw * D * 2 if world > 1 else 0,
+        "algorithmic_bytes_per_step": total,
+    }
+
+
 def cpu_attention_baseline(state, budget_s: float = 12.0):
     """The reference's unfused op (dequantize in bf16, expand GQA heads,
     boolean mask, SDPA) restated with CPU torch, over as many of the
@@ -513,6 +590,10 @@ def main(argv=None) -> int:
     if not args.skip_append:
         append = run_append(args.seed + 1000 * rank, device, args.steps, args.warmup, world, flush)
 
+    long_ctx = None
+    if not args.skip_long:
+        long_ctx = run_long_context(args.seed, rank, world, device, args.steps, args.warmup)
+
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         cpu = cpu_attention_baseline(state)
@@ -545,8 +626,9 @@ def main(argv=None) -> int:
                          "traffic": profiled_traffic("verify_attention_8b"),
                          "algorithmic_bytes_per_launch": state["bytes"]},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "append": append,
+            "long_context_70b": long_ctx,
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
