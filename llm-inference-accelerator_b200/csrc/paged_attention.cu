@@ -263,50 +263,70 @@ template <>
 __device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
 
 // Merges the chunk partials of one (sequence, KV head) and writes the output.
-// Row weights exp2(m_c - m) / L are computed once per (chunk, row) into shared
-// memory; the head_dim sweep is then one coalesced load and FMA per chunk.
-constexpr int kCombineThreads = 256;
-constexpr int kCombineMaxWeights = 12 * 1024;  // 48 KiB of float weights
+// One coalesced pass brings every chunk's (m, l) into shared memory; thread r
+// < rows turns them into the row's weights exp2(m_c - m) / L; then each thread
+// owns four head-dim columns of a row and sums chunk partials with 16-byte
+// loads, so the block waits for about three memory round trips in all.
+constexpr int kCombineThreads = 128;
+constexpr int kCombineMaxWeights = 12 * 1024;  // chunks x rows; 3 floats each in shared memory
 
 template <typename QT>
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(AttnArgs a) {
-    __shared__ float weights[kCombineMaxWeights];
+    extern __shared__ float csm[];  // ml [chunks][rows][2], then weights [chunks][rows]
     const int64_t item = blockIdx.x;
     const int64_t b = item / a.kv_heads;
     const int64_t h = item - b * a.kv_heads;
     const int R = static_cast<int>(a.rows);
-    const int64_t D = a.head_dim;
+    const int D = static_cast<int>(a.head_dim);
     const int64_t T = __ldg(a.context_lens + b);
     QT* out = static_cast<QT*>(a.out) + ((b * a.query_heads + h * a.group) * a.window) * D;
     const bool valid_ctx = T >= a.window && T <= a.table_stride * a.pool.block_size &&
                            T <= a.max_chunks * a.chunk;
     if (!valid_ctx) {
-        for (int64_t idx = threadIdx.x; idx < R * D; idx += blockDim.x) out[idx] = from_float<QT>(0.0f);
+        for (int idx = threadIdx.x; idx < R * D; idx += blockDim.x) out[idx] = from_float<QT>(0.0f);
         return;
     }
-    const int64_t chunks = (T + a.chunk - 1) / a.chunk;
+    const int chunks = static_cast<int>((T + a.chunk - 1) / a.chunk);
     const float* ml = a.part_ml + item * a.max_chunks * R * 2;
     const float* po = a.part_o + item * a.max_chunks * R * D;
-    // the host keeps chunks * rows within the weight buffer
+    float* weights = csm + 2 * chunks * R;
+    // the host keeps chunks * rows within kCombineMaxWeights
+    for (int i = threadIdx.x; i < 2 * chunks * R; i += blockDim.x) csm[i] = __ldg(ml + i);
+    __syncthreads();
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
         float m = -INFINITY;
-        for (int64_t c = 0; c < chunks; ++c) m = fmaxf(m, ml[(c * R + r) * 2]);
+        for (int c = 0; c < chunks; ++c) m = fmaxf(m, csm[(c * R + r) * 2]);
         float l = 0.0f;
-        for (int64_t c = 0; c < chunks; ++c) {
-            const float mc = ml[(c * R + r) * 2];
+        for (int c = 0; c < chunks; ++c) {
+            const float mc = csm[(c * R + r) * 2];
             const float w = mc == -INFINITY ? 0.0f : exp2f(mc - m);
             weights[c * R + r] = w;
-            l = fmaf(ml[(c * R + r) * 2 + 1], w, l);
+            l = fmaf(csm[(c * R + r) * 2 + 1], w, l);
         }
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        for (int64_t c = 0; c < chunks; ++c) weights[c * R + r] *= inv;
+        for (int c = 0; c < chunks; ++c) weights[c * R + r] *= inv;
     }
     __syncthreads();
-    for (int64_t idx = threadIdx.x; idx < R * D; idx += blockDim.x) {
-        const int64_t r = idx / D;
-        float o = 0.0f;
-        for (int64_t c = 0; c < chunks; ++c) o = fmaf(po[c * R * D + idx], weights[c * R + r], o);
-        out[idx] = from_float<QT>(o);
+    // D / 4 threads cover a row, 4 columns each (16-byte loads); the block
+    // sweeps 4 * blockDim / D rows per pass
+    const int per_row = D / 4;
+    const int rows_per_pass = blockDim.x / per_row;
+    const int d4 = (threadIdx.x % per_row) * 4;
+    for (int r = threadIdx.x / per_row; r < R; r += rows_per_pass) {
+        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int c = 0; c < chunks; ++c) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(po + (static_cast<int64_t>(c) * R + r) * D + d4));
+            const float w = weights[c * R + r];
+            o.x = fmaf(v.x, w, o.x);
+            o.y = fmaf(v.y, w, o.y);
+            o.z = fmaf(v.z, w, o.z);
+            o.w = fmaf(v.w, w, o.w);
+        }
+        QT* dst = out + r * D + d4;
+        dst[0] = from_float<QT>(o.x);
+        dst[1] = from_float<QT>(o.y);
+        dst[2] = from_float<QT>(o.z);
+        dst[3] = from_float<QT>(o.w);
     }
 }
 
@@ -338,7 +358,12 @@ sdc_status_t launch_simt_rows(const AttnArgs& a, int rpw, dim3 grid, size_t smem
 
 template <typename QT>
 sdc_status_t launch_combine_typed(const AttnArgs& a, cudaStream_t st) {
-    attn_combine_kernel<QT><<<static_cast<unsigned>(a.batch * a.kv_heads), kCombineThreads, 0, st>>>(a);
+    const size_t smem = static_cast<size_t>(a.max_chunks * a.rows) * 3 * sizeof(float);
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(attn_combine_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem)) != cudaSuccess) {
+        return SDC_STATUS_CUDA_ERROR;
+    }
+    attn_combine_kernel<QT><<<static_cast<unsigned>(a.batch * a.kv_heads), kCombineThreads, smem, st>>>(a);
     return launch_status();
 }
 
