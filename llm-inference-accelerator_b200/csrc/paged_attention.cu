@@ -273,6 +273,7 @@ constexpr int kCombineMaxWeights = 12 * 1024;  // chunks x rows; 3 floats each i
 template <typename QT>
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(AttnArgs a) {
     extern __shared__ float csm[];  // ml [chunks][rows][2], then weights [chunks][rows]
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // partials of the item kernel (no-op for a plain launch)
     const int64_t item = blockIdx.x;
     const int64_t b = item / a.kv_heads;
     const int64_t h = item - b * a.kv_heads;
@@ -357,13 +358,23 @@ sdc_status_t launch_simt_rows(const AttnArgs& a, int rpw, dim3 grid, size_t smem
 }
 
 template <typename QT>
-sdc_status_t launch_combine_typed(const AttnArgs& a, cudaStream_t st) {
+sdc_status_t launch_combine_typed(const AttnArgs& a, cudaStream_t st, bool programmatic) {
     const size_t smem = static_cast<size_t>(a.max_chunks * a.rows) * 3 * sizeof(float);
     if (smem > 48 * 1024 && cudaFuncSetAttribute(attn_combine_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(smem)) != cudaSuccess) {
         return SDC_STATUS_CUDA_ERROR;
     }
-    attn_combine_kernel<QT><<<static_cast<unsigned>(a.batch * a.kv_heads), kCombineThreads, smem, st>>>(a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.kv_heads));
+    cfg.blockDim = dim3(kCombineThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = programmatic ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, attn_combine_kernel<QT>, a) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
     return launch_status();
 }
 
@@ -381,7 +392,7 @@ sdc_status_t launch_simt_typed(const AttnArgs& a, cudaStream_t st) {
         default: return SDC_STATUS_UNSUPPORTED;
     }
     if (rc != SDC_STATUS_OK) return rc;
-    return launch_combine_typed<QT>(a, st);
+    return launch_combine_typed<QT>(a, st, false);
 }
 
 }  // namespace
@@ -393,11 +404,11 @@ bool simt_supports(int64_t head_dim, int64_t rows) {
            rows <= kWarps * 8;
 }
 
-sdc_status_t launch_attention_combine(const AttnArgs& a, cudaStream_t st) {
+sdc_status_t launch_attention_combine(const AttnArgs& a, cudaStream_t st, bool programmatic) {
     switch (a.query_dtype) {
-        case SDC_DTYPE_BF16: return launch_combine_typed<__nv_bfloat16>(a, st);
-        case SDC_DTYPE_F16: return launch_combine_typed<__half>(a, st);
-        case SDC_DTYPE_F32: return launch_combine_typed<float>(a, st);
+        case SDC_DTYPE_BF16: return launch_combine_typed<__nv_bfloat16>(a, st, programmatic);
+        case SDC_DTYPE_F16: return launch_combine_typed<__half>(a, st, programmatic);
+        case SDC_DTYPE_F32: return launch_combine_typed<float>(a, st, programmatic);
         default: return SDC_STATUS_UNSUPPORTED;
     }
 }

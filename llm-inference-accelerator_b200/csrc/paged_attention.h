@@ -35,7 +35,9 @@ struct AttnArgs {
 bool simt_supports(int64_t head_dim, int64_t rows);
 sdc_status_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream);
 // Merges the per-chunk partials into the output (used by both item kernels).
-sdc_status_t launch_attention_combine(const AttnArgs& a, cudaStream_t stream);
+// `programmatic`: launched as a programmatic dependent of the item kernel
+// (it waits for that grid's results with griddepcontrol.wait).
+sdc_status_t launch_attention_combine(const AttnArgs& a, cudaStream_t stream, bool programmatic = false);
 // Whether max_chunks * rows chunk weights fit the combine's shared buffer.
 bool combine_fits(int64_t max_chunks, int64_t rows);
 

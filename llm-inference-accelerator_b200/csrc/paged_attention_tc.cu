@@ -321,8 +321,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int count = __ldg(t.item_count);
-    if (static_cast<int>(blockIdx.x) >= count) return;  // whole block: no work
+    // launched programmatically after the planning launch: set up barriers
+    // and tensor memory while it finishes, read its outputs only after
+    // griddepcontrol.wait; the combine launch may start its own set-up now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kBarOff);
     auto bar = [&](int i) { return smem_u32(bars + i); };
@@ -376,6 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_base_slot;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the work list and query images are written
+    const int count = __ldg(t.item_count);
 
     const uint32_t stage_base = smem_u32(smem + LY::kStageOff);
     const uint32_t q_base = smem_u32(smem + LY::kQOff);
@@ -383,7 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t bs = a.pool.block_size;
     const int pages_per_tile = static_cast<int>(kTile / bs);
 
-    if (warp == kKeyWarp || warp == kValueWarp || warp == kScaleWarp) {
+    if (static_cast<int>(blockIdx.x) >= count) {
+        // no item for this block: straight to the teardown
+    } else if (warp == kKeyWarp || warp == kValueWarp || warp == kScaleWarp) {
         // ------------------------------------------------------------ copies
         // Three warps share the copies of a tile, each arriving on the
         // stage's full barrier with its own bytes: warp 8 the key codes and
@@ -922,6 +928,7 @@ template <int RB>
 __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
     using LY = Rows<RB>;
     const AttnArgs& a = t.a;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the item kernel may start its set-up
     if (blockIdx.x > 0) {
         const int lane = threadIdx.x & 31;
         const int64_t w = static_cast<int64_t>(blockIdx.x - 1) * 32 + (threadIdx.x >> 5);
@@ -1137,7 +1144,17 @@ sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUten
     }
     const int64_t max_items = t.a.batch * t.a.kv_heads * t.a.max_chunks * t.splits;
     const int64_t grid = std::min<int64_t>(num_sms(), max_items);
-    kernel<<<static_cast<unsigned>(grid), kThreads, LY::kDynamicSmem, st>>>(kmap, vmap, ksmap, vsmap, t);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = LY::kDynamicSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kernel, kmap, vmap, ksmap, vsmap, t) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
     return launch_status();
 }
 
@@ -1210,7 +1227,7 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
         default: return SDC_STATUS_UNSUPPORTED;
     }
     if (rc != SDC_STATUS_OK) return rc;
-    return launch_attention_combine(a, st);
+    return launch_attention_combine(a, st, /*programmatic=*/true);
 }
 
 }  // namespace tc
