@@ -49,6 +49,42 @@ __device__ __forceinline__ int quant_one(typename AccOf<Src>::type x, float s, f
     }
 }
 
+// Sixteen codes of a float-valued vector with scale s >= 2^-100 (rcp = 1/s
+// rounded), packed four to a word: round_half_away(x / s) clamped to 127 in
+// magnitude, the same integers as quant_code_f32 but with no conversion
+// instruction.  The candidate rint(|x| * rcp) comes from adding and removing
+// 1.5 * 2^23 (round to nearest even of a value below 2^22, exactly what rintf
+// returns); it is within one of the answer and is corrected by the exact
+// signs of |x| - (n +- 1/2) s, each from one fused multiply-add.  The signed
+// code plus 1.5 * 2^23 holds the code's two's-complement byte in its low
+// mantissa bits, which byte permutes pack.  Pairs of elements go through the
+// packed f32x2 arithmetic.
+__device__ __forceinline__ uint4 quant16_f32(const float (&x)[16], float s, float rcp) {
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    const float2 rcp2 = make_float2(rcp, rcp), negs2 = make_float2(-s, -s);
+    const float2 m2 = make_float2(kMagic, kMagic), negm2 = make_float2(-kMagic, -kMagic);
+    const float2 half2 = make_float2(0.5f, 0.5f), neghalf2 = make_float2(-0.5f, -0.5f);
+    uint32_t bits[16];
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+        const float2 a = make_float2(fabsf(x[i]), fabsf(x[i + 1]));
+        float2 n = __fadd2_rn(__fadd2_rn(__fmul2_rn(a, rcp2), m2), negm2);
+        const float2 above = __ffma2_rn(__fadd2_rn(n, half2), negs2, a);     // a - (n + 1/2) s
+        const float2 below = __ffma2_rn(__fadd2_rn(n, neghalf2), negs2, a);  // a - (n - 1/2) s
+        n.x += (above.x >= 0.0f ? 1.0f : 0.0f) - (below.x < 0.0f ? 1.0f : 0.0f);
+        n.y += (above.y >= 0.0f ? 1.0f : 0.0f) - (below.y < 0.0f ? 1.0f : 0.0f);
+        const float2 q = make_float2(copysignf(fminf(n.x, 127.0f), x[i]), copysignf(fminf(n.y, 127.0f), x[i + 1]));
+        const float2 t = __fadd2_rn(q, m2);
+        bits[i] = __float_as_uint(t.x);
+        bits[i + 1] = __float_as_uint(t.y);
+    }
+    auto pack = [](uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+        return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
+    };
+    return make_uint4(pack(bits[0], bits[1], bits[2], bits[3]), pack(bits[4], bits[5], bits[6], bits[7]),
+                      pack(bits[8], bits[9], bits[10], bits[11]), pack(bits[12], bits[13], bits[14], bits[15]));
+}
+
 // Per-group maximum of |x| over 16 elements per lane and LPV lanes; for float
 // sources a non-finite element makes the result NaN or +inf.
 template <typename Src, int LPV>
@@ -153,19 +189,33 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
     float s = 0.0f;
     uint4 packed = make_uint4(0u, 0u, 0u, 0u);
     if (m != Acc(0)) {
-        s = scale_from_max(static_cast<double>(m));
+        if constexpr (std::is_same<Src, double>::value) {
+            s = scale_from_max(m);
+        } else {
+            // for a float maximum the reference's double quotient rounded to
+            // float equals the correctly rounded float quotient (53 >= 2 * 24 + 2
+            // bits: double rounding of a division is innocuous)
+            s = __fdiv_rn(m, 127.0f);
+        }
         if (!(s > 0.0f) || isinf(s)) {
             if (sub == 0) report_fault(a.status, SDC_FAULT_INVALID_SCALE);
             return;
         }
         const float rcp = 1.0f / s;
-        int q[16];
+        if (!std::is_same<Src, double>::value && s >= kFloatPathMinScale) {
+            float xf[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) q[i] = quant_one<Src>(x[i], s, rcp);
-        packed.x = pack4(q[0], q[1], q[2], q[3]);
-        packed.y = pack4(q[4], q[5], q[6], q[7]);
-        packed.z = pack4(q[8], q[9], q[10], q[11]);
-        packed.w = pack4(q[12], q[13], q[14], q[15]);
+            for (int i = 0; i < 16; ++i) xf[i] = static_cast<float>(x[i]);
+            packed = quant16_f32(xf, s, rcp);
+        } else {
+            int q[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) q[i] = quant_one<Src>(x[i], s, rcp);
+            packed.x = pack4(q[0], q[1], q[2], q[3]);
+            packed.y = pack4(q[4], q[5], q[6], q[7]);
+            packed.z = pack4(q[8], q[9], q[10], q[11]);
+            packed.w = pack4(q[12], q[13], q[14], q[15]);
+        }
     }
     if (has_chunk) *reinterpret_cast<uint4*>(codes + sub * 16) = packed;
     if (sub == 0) *scale_dst = s;
