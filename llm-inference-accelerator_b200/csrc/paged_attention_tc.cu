@@ -344,8 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar(qEmpty + i), 1 + 4 * kGroups);
             mbar_init(bar(sFull + i), 1);
             mbar_init(bar(sEmpty + i), 4);
-            mbar_init(bar(pFull + 2 * i), 128);
-            mbar_init(bar(pFull + 2 * i + 1), 128);
+            mbar_init(bar(pFull + 2 * i), 4);  // one arrival per warp of the group
+            mbar_init(bar(pFull + 2 * i + 1), 4);
             mbar_init(bar(oFull + i), 1);
             mbar_init(bar(oEmpty + i), 4);
         }
@@ -831,8 +831,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<uint4*>(prow + c * 2048) =
                         make_uint4(words[4 * c], words[4 * c + 1], words[4 * c + 2], words[4 * c + 3]);
                 }
+                // every thread orders its P stores before the tensor core's
+                // reads; the warp's lane 0 then arrives for all 32
                 fence_proxy_async();
-                mbar_arrive(bar(pFull + grp * 2 + (own & 1)));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(pFull + grp * 2 + (own & 1)));
 
                 if (have_prev && !epilogue(prev_own, vf_prev, o_acc)) {
                     ok = false;
