@@ -55,6 +55,9 @@ def parse_args(argv=None):
     p.add_argument("--skip-append", action="store_true", help="measure only the verify attention")
     p.add_argument("--skip-cpu-baseline", action="store_true")
     p.add_argument("--skip-long", action="store_true", help="skip the 70B long-context (KV-head parallel) workload")
+    p.add_argument("--profile-append", action="store_true",
+                   help="the append workload's step (256 sequences x 5 tokens, 32 layers) on a 4096-block pool, "
+                        "a few steps, no timing: small enough for a full ncu capture")
     p.add_argument("--profile", action="store_true",
                    help="verify attention only: no clock sampling, sustained load, host-buffer pass, append "
                         "workload or CPU baseline (a short, repeatable run for ncu)")
@@ -397,6 +400,39 @@ def run_append(seed: int, device, steps: int, warmup: int, world: int, flush):
 # CPU baseline (the reference's CPU path, bounded sample)
 # ---------------------------------------------------------------------------
 
+def profile_append(seed: int, device, steps: int) -> None:
+    """The append / rollback step of the append workload on a small pool."""
+    import numpy as np
+    import torch
+
+    from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
+
+    a = APPEND
+    nb = 4096
+    rng = np.random.default_rng(seed + 1)
+    cache = PagedKVCache(KVCacheConfig(a["layers"], a["kv_heads"], a["head_dim"], block_size=a["block_size"],
+                                       num_blocks=nb),
+                         device=device, block_order=rng.permutation(nb), max_sequences=a["sequences"],
+                         max_blocks_per_sequence=16, check_status=False)
+    seqs = list(range(a["sequences"]))
+    for s in seqs:
+        cache.create_sequence(s)
+    gen = torch.Generator(device=device).manual_seed(seed + 2)
+    shape = (a["sequences"], a["window"], a["layers"], a["kv_heads"], a["head_dim"])
+    factors = torch.exp(torch.empty((1, 1, 1, a["kv_heads"], 1), device=device).uniform_(
+        math.log(0.1), math.log(10.0), generator=gen))
+    keys = (torch.randn(shape, generator=gen, device=device) * factors).to(torch.bfloat16)
+    values = (torch.randn(shape, generator=gen, device=device) * factors).to(torch.bfloat16)
+    for _ in range(steps):
+        cache.append_batch(seqs, keys, values)
+        rolled = rng.integers(0, a["window"] + 1, size=a["sequences"])
+        cache.truncate_batch(seqs, [cache.sequence_length(s) - int(r) for s, r in zip(seqs, rolled)])
+    torch.cuda.synchronize()
+    if cache.status_bits():
+        raise RuntimeError("device fault in the append profile run")
+    print(json.dumps({"profile_append": True, "steps": steps}))
+
+
 def run_long_context(seed: int, rank: int, world: int, device, steps: int, warmup: int):
     """Llama-3.1-70B long-context verify, one layer: 8 sequences x 131072
     tokens, 64 query / 8 KV heads, window 5.  KV heads are split over the
@@ -549,6 +585,9 @@ def main(argv=None) -> int:
     import torch
 
     device = torch.device("cuda", local)
+    if args.profile_append:
+        profile_append(args.seed, device, args.steps + args.warmup)
+        return 0
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
     state = build_verify(args.seed + 1000 * rank, device)
 
