@@ -60,6 +60,8 @@ constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
 // A KV head's query rows (GQA group x window) beyond 32 are split over up
 // to kMaxSplits items per chunk, each serving at most 32 rows.
 constexpr int kMaxSplits = 2;
+// Largest work item in tiles (the chunk size is clamped to 16384 tokens).
+constexpr int kMaxItemTiles = 16384 / kTile;
 
 template <int RB>
 struct Rows {
@@ -380,6 +382,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_base_slot;
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the work list and query images are written
     const int count = __ldg(t.item_count);
+    // The work list is sorted by size, largest first; block c takes
+    // positions c, 2 grid - 1 - c, 2 grid + c, ... (snake order), which
+    // balances the blocks' total work.
+    auto item_pos = [&](int k) -> int {
+        const int grid = static_cast<int>(gridDim.x);
+        return k * grid + ((k & 1) ? grid - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x));
+    };
 
     const uint32_t stage_base = smem_u32(smem + LY::kStageOff);
     const uint32_t q_base = smem_u32(smem + LY::kQOff);
@@ -405,10 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int lg_bs = __ffs(static_cast<int>(bs)) - 1;  // block sizes are powers of two
         const bool gather = t.gather4 != 0;
         uint32_t g = 0, li = 0, q_issued = 0;
-        WorkItem nxt = t.items[blockIdx.x];
-        for (int item = blockIdx.x; item < count; item += gridDim.x, ++li) {
+        WorkItem nxt = t.items[item_pos(0)];
+        for (int k = 0, item = item_pos(0); item < count; ++k, item = item_pos(k), ++li) {
             const WorkItem it = nxt;
-            if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
+            if (item_pos(k + 1) < count) nxt = t.items[item_pos(k + 1)];
             if (scale_side) {
                 const uint32_t qb = li & 1;
                 if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status)) break;
@@ -508,10 +517,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t kIdescO = idesc_i8(kHeadDim, N, 1, 1);
         if (lane == 0) {
             uint32_t gs = 0, gp = 0, li = 0;
-            int item = blockIdx.x;
+            int k = 0;
+            int item = item_pos(0);
             WorkItem it = t.items[item];
             WorkItem nxt = it;
-            if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
+            if (item_pos(1) < count) nxt = t.items[item_pos(1)];
             int tile0 = it.t0;
             bool s_done = false, q_ready = false;
             long long idle_since = cycles();
@@ -539,14 +549,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tile0 += kTile;
                         if (tile0 >= it.t1) {  // the item's last tile: its query image is free once this lands
                             mma_commit(bar(qEmpty + qb));
-                            item += gridDim.x;
+                            item = item_pos(++k);
                             ++li;
                             q_ready = false;
                             if (item >= count) {
                                 s_done = true;
                             } else {
                                 it = nxt;
-                                if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
+                                if (item_pos(k + 1) < count) nxt = t.items[item_pos(k + 1)];
                                 tile0 = it.t0;
                             }
                         }
@@ -660,10 +670,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
 
         bool ok = true;
-        WorkItem nxt = t.items[blockIdx.x];
-        for (int item = blockIdx.x; item < count && ok; item += gridDim.x, ++li) {
+        WorkItem nxt = t.items[item_pos(0)];
+        for (int k = 0, item = item_pos(0); item < count && ok; ++k, item = item_pos(k), ++li) {
             const WorkItem it = nxt;
-            if (item + static_cast<int>(gridDim.x) < count) nxt = t.items[item + gridDim.x];
+            if (item_pos(k + 1) < count) nxt = t.items[item_pos(k + 1)];
             const uint32_t qb = li & 1;
             if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status)) break;
             const float* qfac = reinterpret_cast<const float*>(smem + LY::kQOff + qb * LY::kQBufBytes + LY::kQCodes);
@@ -919,9 +929,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// Planning launch.  Block 0 writes the work list: (sequence, KV head, chunk)
-// items, sequences in order; sequences whose context length is invalid get
-// no items (the combine writes zeros).  Every other block quantizes query
+// Planning launch.  Block 0 writes the work list: (sequence, KV head, chunk,
+// row split) items sorted by size, largest first; sequences whose context
+// length is invalid get no items (the combine writes zeros).  Every other block quantizes query
 // rows, one warp per (sequence, KV head, row): each row splits into INT8
 // hi / lo parts written in the score MMA's B layout (K-major, no swizzle:
 // 8 rows x 16 bytes per 128-byte core matrix, 16-byte K chunks 128 bytes
@@ -994,39 +1004,46 @@ __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
         return;
     }
 
-    using Scan = cub::BlockScan<int32_t, 1024>;
-    __shared__ typename Scan::TempStorage temp;
-    __shared__ int32_t carry;
-    if (threadIdx.x == 0) carry = 0;
+    // Work list sorted by size (tiles per item), largest first: a counting
+    // sort over the at most kMaxItemTiles + 1 sizes.  A chunk's row splits
+    // take adjacent positions, so they run on neighbouring SMs at about the
+    // same time and the second reads its pages from L2.
+    __shared__ int32_t hist[kMaxItemTiles + 1];
+    for (int i = threadIdx.x; i <= kMaxItemTiles; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int64_t base = 0; base < a.batch; base += 1024) {
-        const int64_t b = base + threadIdx.x;
-        int32_t n = 0;
-        if (b < a.batch) {
-            const int64_t T = __ldg(a.context_lens + b);
-            const bool valid =
-                T >= a.window && T <= a.table_stride * a.pool.block_size && T <= a.max_chunks * a.chunk;
-            if (!valid) report_fault(a.status, SDC_FAULT_CONTEXT_RANGE);
-            n = valid ? static_cast<int32_t>(((T + a.chunk - 1) / a.chunk) * a.kv_heads * t.splits) : 0;
-        }
-        int32_t off, total;
-        Scan(temp).ExclusiveSum(n, off, total);
-        if (b < a.batch) first[b] = carry + off;
-        __syncthreads();
-        if (threadIdx.x == 0) carry += total;
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) *const_cast<int32_t*>(t.item_count) = carry;
+    auto valid_len = [&](int64_t T) {
+        return T >= a.window && T <= a.table_stride * a.pool.block_size && T <= a.max_chunks * a.chunk;
+    };
+    auto tiles_of = [&](int64_t T, int64_t c) {
+        return static_cast<int>((min(T, (c + 1) * a.chunk) - c * a.chunk + kTile - 1) / kTile);
+    };
+    const int per_chunk = static_cast<int>(a.kv_heads) * t.splits;
     for (int64_t b = threadIdx.x; b < a.batch; b += blockDim.x) {
         const int64_t T = __ldg(a.context_lens + b);
-        const bool valid = T >= a.window && T <= a.table_stride * a.pool.block_size && T <= a.max_chunks * a.chunk;
-        if (!valid) continue;
-        const int64_t chunks = (T + a.chunk - 1) / a.chunk;
-        WorkItem* out = const_cast<WorkItem*>(t.items) + first[b];
-        // the splits of one chunk are adjacent, so they run on neighbouring
-        // SMs at about the same time and the second reads its pages from L2
-        for (int64_t c = 0; c < chunks; ++c) {
+        if (!valid_len(T)) {
+            report_fault(a.status, SDC_FAULT_CONTEXT_RANGE);
+            continue;
+        }
+        for (int64_t c = 0; c * a.chunk < T; ++c) atomicAdd(&hist[tiles_of(T, c)], per_chunk);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // bin start positions, largest size first
+        int32_t running = 0;
+        for (int i = kMaxItemTiles; i >= 1; --i) {
+            const int32_t n = hist[i];
+            hist[i] = running;
+            running += n;
+        }
+        *const_cast<int32_t*>(t.item_count) = running;
+    }
+    __syncthreads();
+    for (int64_t b = threadIdx.x; b < a.batch; b += blockDim.x) {
+        const int64_t T = __ldg(a.context_lens + b);
+        if (!valid_len(T)) continue;
+        for (int64_t c = 0; c * a.chunk < T; ++c) {
+            const int tiles = tiles_of(T, c);
             for (int64_t h = 0; h < a.kv_heads; ++h) {
+                const int32_t pos = atomicAdd(&hist[tiles], t.splits);
                 for (int sp = 0; sp < t.splits; ++sp) {
                     WorkItem w;
                     w.b = static_cast<int32_t>(b);
@@ -1037,11 +1054,12 @@ __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
                     w.chunk = static_cast<int32_t>(c);
                     w.split = sp;
                     w.pad = 0;
-                    out[(c * a.kv_heads + h) * t.splits + sp] = w;
+                    const_cast<WorkItem*>(t.items)[pos + sp] = w;
                 }
             }
         }
     }
+    (void)first;
 }
 
 // ---------------------------------------------------------------- host side
@@ -1183,7 +1201,7 @@ int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len, int6
     int64_t c = (batch * kv_heads * splits_for(rows) * max_context_len + slots - 1) / slots;
     c = (c + kTile - 1) / kTile * kTile;
     if (c < 512) c = 512;
-    if (c > 16384) c = 16384;
+    if (c > kMaxItemTiles * kTile) c = kMaxItemTiles * kTile;
     return c;
 }
 
