@@ -1,0 +1,129 @@
+"""Hugging Face attention hook over the paged INT8 cache.
+
+Replaces the reference's CPU reconstruct path for a transformers model
+(src/specdecode/huggingface.py:382-393 rebuilds a legacy cache from the
+paged mirror with ``materialize_like`` before every forward, and
+src/specdecode/hf_paged_cache.py:199-232 mirrors new keys / values through
+``.tolist()``): with the hook installed, every attention layer of the model
+quantizes its new keys and values straight into the device page pool
+(kernel (a), one layer at a time) and attends over the pool with the fused
+paged attention kernel (c).  The model runs with ``use_cache=False``; the
+page pool is its only cache.
+
+Usage::
+
+    session = PagedAttentionSession(cache)          # a PagedKVCache with the model's geometry
+    model.set_attn_implementation(PagedAttentionSession.NAME)
+    with session.step(sequence_ids, new_tokens):
+        logits = model(input_ids, position_ids=positions, use_cache=False).logits
+
+``step`` reserves the new tokens' slots for every layer first.  Each listed
+sequence contributes the same number of new tokens, its queries sit at the
+end of its own context (the paged cache carries every sequence's length, so
+padding masks are neither needed nor supported), and positions must be
+``range(length, length + new_tokens)`` per sequence.  Queries too large for
+one kernel call (a prefill: query heads per KV head x new tokens above 64
+rows) run as consecutive causal windows, each over the context up to its
+last position.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import math
+from typing import Hashable, Sequence
+
+from .cuda_kv_cache import PagedVerifyAttention
+from .kv_cache import PagedKVCache
+
+_ACTIVE: list["PagedAttentionSession"] = []
+_MAX_ROWS = 64  # query rows per KV head one kernel call serves
+
+
+class PagedAttentionError(RuntimeError):
+    """The model's attention call does not match the paged cache."""
+
+
+def _attention_forward(module, query, key, value, attention_mask, dropout: float = 0.0, scaling=None, **kwargs):
+    if not _ACTIVE:
+        raise PagedAttentionError("paged attention used outside PagedAttentionSession.step()")
+    return _ACTIVE[-1].forward(module, query, key, value, scaling, dropout)
+
+
+def _no_mask(*args, **kwargs):
+    return None
+
+
+def register() -> None:
+    """Register the hook's attention and (empty) mask functions with transformers."""
+    from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface
+
+    AttentionInterface.register(PagedAttentionSession.NAME, _attention_forward)
+    AttentionMaskInterface.register(PagedAttentionSession.NAME, _no_mask)
+
+
+class PagedAttentionSession:
+    """Routes a model's attention layers through one ``PagedKVCache``."""
+
+    NAME = "specdecode_paged"
+
+    def __init__(self, cache: PagedKVCache) -> None:
+        self.cache = cache
+        self.attention = PagedVerifyAttention.for_cache(cache)
+        self._pending = None
+        self._ids: list[Hashable] = []
+        self._new = 0
+        self._inputs = None
+        register()
+
+    @contextlib.contextmanager
+    def step(self, sequence_ids: Sequence[Hashable], new_tokens: int):
+        """Reserve ``new_tokens`` slots per sequence, then run the model inside
+        the block.  Every layer must be written by the forward pass."""
+        if self._pending is not None:
+            raise PagedAttentionError("a step is already open")
+        self._ids = list(sequence_ids)
+        self._new = int(new_tokens)
+        self._pending = self.cache.reserve(self._ids, self._new)
+        self._inputs = self.cache.attention_inputs(self._ids)
+        _ACTIVE.append(self)
+        try:
+            yield self
+        finally:
+            _ACTIVE.remove(self)
+            self._pending = None
+            self._inputs = None
+        self.cache.check_status()
+
+    def forward(self, module, query, key, value, scaling, dropout):
+        import torch
+
+        if dropout:
+            raise PagedAttentionError("paged attention has no dropout")
+        B, Hq, q_len, D = (int(d) for d in query.shape)
+        Hkv = int(key.shape[1])
+        if B != len(self._ids) or q_len != self._new:
+            raise PagedAttentionError(
+                f"attention over {B} x {q_len} new tokens, but the step reserved {len(self._ids)} x {self._new}")
+        if scaling is not None and not math.isclose(float(scaling), 1.0 / math.sqrt(D), rel_tol=1e-6):
+            raise PagedAttentionError("paged attention uses the 1/sqrt(head_dim) softmax scale")
+        layer = int(module.layer_idx)
+        # this layer's new keys / values, sequence-major: [B * q_len, Hkv, D]
+        k = key.transpose(1, 2).reshape(B * q_len, Hkv, D)
+        v = value.transpose(1, 2).reshape(B * q_len, Hkv, D)
+        self.cache.write_layer(self._pending, layer, k, v)
+        tables, lens, max_len = self._inputs
+        group = Hq // Hkv
+        window = max(1, _MAX_ROWS // group)
+        if q_len <= window:
+            out = self.attention(query.contiguous(), tables, lens, max_len, layer)
+        else:
+            parts = []
+            for j in range(0, q_len, window):
+                w = min(window, q_len - j)
+                behind = q_len - (j + w)  # new tokens after this window
+                parts.append(self.attention(query[:, :, j:j + w].contiguous(), tables, lens - behind,
+                                            max_len - behind, layer))
+            out = torch.cat(parts, dim=2)
+        return out.transpose(1, 2).contiguous(), None

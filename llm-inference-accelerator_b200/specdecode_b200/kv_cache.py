@@ -253,6 +253,16 @@ class PendingAppend:
 
 
 @dataclass
+class LayerwiseAppend:
+    """Slots reserved for new tokens of every layer (``PagedKVCache.reserve``),
+    filled one layer at a time by ``PagedKVCache.write_layer``."""
+
+    plan: AppendPlan
+    slots: object  # device int64 [tokens], sequence-major
+    tokens: int
+
+
+@dataclass
 class PendingTruncate:
     plan: TruncatePlan
     pointers: list | None
@@ -457,6 +467,60 @@ class PagedKVCache:
             self._meta.release(ticket, stream)
         self._lib.check(status, "rollback")
         self._pages.undo_append(plan)
+
+    def reserve(self, sequence_ids: Sequence[Hashable], count: int) -> LayerwiseAppend:
+        """Allocate pages for ``count`` new tokens of every listed sequence and
+        extend their device block tables and lengths without writing codes.
+        ``write_layer`` then quantizes each layer's keys / values into the
+        reserved slots, which is how a model whose layers run one after
+        another (an attention hook) appends; a layer's attention over the new
+        tokens is valid once that layer has been written.  Capacity is checked
+        first: a failed reservation changes nothing."""
+        torch = _torch()
+        ids = list(sequence_ids)
+        count = int(count)
+        if count < 1:
+            raise ValueError("reserve at least one token")
+        plan = self._pages.plan_append(ids, [count] * len(ids))
+        stream = self._stream()
+        try:
+            slots = torch.from_numpy(np.ascontiguousarray(plan.slots, dtype=np.int64)).to(self.device)
+            (_, entries_ptr, lengths_ptr), ticket = self._meta.upload(
+                [plan.slots, plan.table_entries, plan.new_lengths], stream)
+        except Exception:
+            self._pages.undo_append(plan)
+            raise
+        edits = self._edits(entries_ptr, len(plan.table_entries), lengths_ptr, len(plan.new_lengths))
+        try:
+            status = self._lib.handle.sdc_quantize_append(
+                self.pool_desc, 0, self.config.num_layers, None, None, _dtype_code(torch.float32), 0, 0, 0, 0,
+                None, edits, self._status.data_ptr(), stream.cuda_stream)
+        finally:
+            self._meta.release(ticket, stream)
+        if status != _lib.STATUS_OK:
+            self._pages.undo_append(plan)
+            self._lib.check(status, "slot reservation")
+        return LayerwiseAppend(plan, slots, int(plan.slots.size))
+
+    def write_layer(self, pending: LayerwiseAppend, layer: int, keys, values) -> None:
+        """Quantize layer ``layer``'s keys / values ``[tokens, num_heads,
+        head_dim]`` (tokens in reservation order: all of the first sequence's,
+        then the next sequence's) into the slots of a reservation."""
+        if not 0 <= int(layer) < self.config.num_layers:
+            raise ValueError(f"layer {layer} outside the cache's {self.config.num_layers} layers")
+        n = pending.tokens
+        H, D = self.config.num_heads, self.config.head_dim
+        if tuple(keys.shape) != (n, H, D) or tuple(values.shape) != (n, H, D):
+            raise ValueError(f"keys/values must have shape [{n}, {H}, {D}]")
+        k = self._as_kv_tensor(keys.reshape(n, 1, H, D), "keys", 1)
+        v = self._as_kv_tensor(values.reshape(n, 1, H, D), "values", 1)
+        if v.dtype != k.dtype:
+            v = v.to(k.dtype)
+        status = self._lib.handle.sdc_quantize_append(
+            self.pool_desc, int(layer), 1, k.data_ptr(), v.data_ptr(), _dtype_code(k.dtype), n,
+            k.stride(0), k.stride(1), k.stride(2), pending.slots.data_ptr(), None, self._status.data_ptr(),
+            self._stream().cuda_stream)
+        self._lib.check(status, "layer write")
 
     def append_tensor(self, sequence_id: Hashable, keys, values) -> tuple[int, ...]:
         """Atomically quantize and append ``keys``/``values`` of shape
