@@ -262,73 +262,84 @@ __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) { re
 template <>
 __device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
 
-// Merges the chunk partials of one (sequence, KV head) and writes the output.
-// One coalesced pass brings every chunk's (m, l) into shared memory; thread r
-// < rows turns them into the row's weights exp2(m_c - m) / L; then each thread
-// owns four head-dim columns of a row and sums chunk partials with 16-byte
-// loads, so the block waits for about three memory round trips in all.
+// Merges the chunk partials of one (sequence, KV head) and a group of its
+// query rows and writes the output.  D / 4 threads cover a row (4 columns
+// each, 16-byte loads), so a block of kCombineThreads serves 4 * 128 / D
+// rows (blockIdx.y picks the group).  One coalesced pass brings the rows'
+// (m, l) of every chunk into shared memory, thread r < rows of the group turns
+// them into weights exp2(m_c - m) / L, and every thread then sums its row's
+// chunk partials with independent loads: about three memory round trips.
 constexpr int kCombineThreads = 128;
-constexpr int kCombineMaxWeights = 12 * 1024;  // chunks x rows; 3 floats each in shared memory
+constexpr int kCombineMaxWeights = 12 * 1024;  // chunks x rows the host admits
 
 template <typename QT>
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(AttnArgs a) {
-    extern __shared__ float csm[];  // ml [chunks][rows][2], then weights [chunks][rows]
+    extern __shared__ float csm[];  // ml [chunks][group rows][2], then weights [chunks][group rows]
     asm volatile("griddepcontrol.wait;" ::: "memory");  // partials of the item kernel (no-op for a plain launch)
     const int64_t item = blockIdx.x;
     const int64_t b = item / a.kv_heads;
     const int64_t h = item - b * a.kv_heads;
     const int R = static_cast<int>(a.rows);
     const int D = static_cast<int>(a.head_dim);
+    const int per_row = D / 4;
+    const int rpb = kCombineThreads / per_row;  // rows of this block's group
+    const int r0 = static_cast<int>(blockIdx.y) * rpb;
+    const int nr = min(rpb, R - r0);
+    if (nr <= 0) return;
     const int64_t T = __ldg(a.context_lens + b);
     QT* out = static_cast<QT*>(a.out) + ((b * a.query_heads + h * a.group) * a.window) * D;
     const bool valid_ctx = T >= a.window && T <= a.table_stride * a.pool.block_size &&
                            T <= a.max_chunks * a.chunk;
+    const int rl = threadIdx.x / per_row;  // this thread's row within the group
+    const int d4 = (threadIdx.x % per_row) * 4;
     if (!valid_ctx) {
-        for (int idx = threadIdx.x; idx < R * D; idx += blockDim.x) out[idx] = from_float<QT>(0.0f);
+        if (rl < nr) {
+            QT* dst = out + (r0 + rl) * D + d4;
+            for (int e = 0; e < 4; ++e) dst[e] = from_float<QT>(0.0f);
+        }
         return;
     }
     const int chunks = static_cast<int>((T + a.chunk - 1) / a.chunk);
     const float* ml = a.part_ml + item * a.max_chunks * R * 2;
     const float* po = a.part_o + item * a.max_chunks * R * D;
-    float* weights = csm + 2 * chunks * R;
-    // the host keeps chunks * rows within kCombineMaxWeights
-    for (int i = threadIdx.x; i < 2 * chunks * R; i += blockDim.x) csm[i] = __ldg(ml + i);
+    float* weights = csm + 2 * chunks * rpb;
+    for (int i = threadIdx.x; i < 2 * chunks * nr; i += blockDim.x) {
+        const int c = i / (2 * nr), j = i - c * 2 * nr;
+        csm[c * 2 * rpb + j] = __ldg(ml + (static_cast<int64_t>(c) * R + r0) * 2 + j);
+    }
     __syncthreads();
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    if (threadIdx.x < nr) {
+        const int r = threadIdx.x;
         float m = -INFINITY;
-        for (int c = 0; c < chunks; ++c) m = fmaxf(m, csm[(c * R + r) * 2]);
+        for (int c = 0; c < chunks; ++c) m = fmaxf(m, csm[(c * rpb + r) * 2]);
         float l = 0.0f;
         for (int c = 0; c < chunks; ++c) {
-            const float mc = csm[(c * R + r) * 2];
+            const float mc = csm[(c * rpb + r) * 2];
             const float w = mc == -INFINITY ? 0.0f : exp2f(mc - m);
-            weights[c * R + r] = w;
-            l = fmaf(csm[(c * R + r) * 2 + 1], w, l);
+            weights[c * rpb + r] = w;
+            l = fmaf(csm[(c * rpb + r) * 2 + 1], w, l);
         }
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        for (int c = 0; c < chunks; ++c) weights[c * R + r] *= inv;
+        for (int c = 0; c < chunks; ++c) weights[c * rpb + r] *= inv;
     }
     __syncthreads();
-    // D / 4 threads cover a row, 4 columns each (16-byte loads); the block
-    // sweeps 4 * blockDim / D rows per pass
-    const int per_row = D / 4;
-    const int rows_per_pass = blockDim.x / per_row;
-    const int d4 = (threadIdx.x % per_row) * 4;
-    for (int r = threadIdx.x / per_row; r < R; r += rows_per_pass) {
-        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int c = 0; c < chunks; ++c) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(po + (static_cast<int64_t>(c) * R + r) * D + d4));
-            const float w = weights[c * R + r];
-            o.x = fmaf(v.x, w, o.x);
-            o.y = fmaf(v.y, w, o.y);
-            o.z = fmaf(v.z, w, o.z);
-            o.w = fmaf(v.w, w, o.w);
-        }
-        QT* dst = out + r * D + d4;
-        dst[0] = from_float<QT>(o.x);
-        dst[1] = from_float<QT>(o.y);
-        dst[2] = from_float<QT>(o.z);
-        dst[3] = from_float<QT>(o.w);
+    if (rl >= nr) return;
+    const int r = r0 + rl;
+    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 4
+    for (int c = 0; c < chunks; ++c) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(po + (static_cast<int64_t>(c) * R + r) * D + d4));
+        const float w = weights[c * rpb + rl];
+        o.x = fmaf(v.x, w, o.x);
+        o.y = fmaf(v.y, w, o.y);
+        o.z = fmaf(v.z, w, o.z);
+        o.w = fmaf(v.w, w, o.w);
     }
+    QT* dst = out + r * D + d4;
+    dst[0] = from_float<QT>(o.x);
+    dst[1] = from_float<QT>(o.y);
+    dst[2] = from_float<QT>(o.z);
+    dst[3] = from_float<QT>(o.w);
 }
 
 template <typename QT, int D>
@@ -359,13 +370,14 @@ sdc_status_t launch_simt_rows(const AttnArgs& a, int rpw, dim3 grid, size_t smem
 
 template <typename QT>
 sdc_status_t launch_combine_typed(const AttnArgs& a, cudaStream_t st, bool programmatic) {
-    const size_t smem = static_cast<size_t>(a.max_chunks * a.rows) * 3 * sizeof(float);
+    const int rpb = kCombineThreads / static_cast<int>(a.head_dim / 4);
+    const size_t smem = static_cast<size_t>(a.max_chunks * rpb) * 3 * sizeof(float);
     if (smem > 48 * 1024 && cudaFuncSetAttribute(attn_combine_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(smem)) != cudaSuccess) {
         return SDC_STATUS_CUDA_ERROR;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.kv_heads));
+    cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.kv_heads), static_cast<unsigned>((a.rows + rpb - 1) / rpb));
     cfg.blockDim = dim3(kCombineThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
