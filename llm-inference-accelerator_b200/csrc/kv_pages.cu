@@ -87,17 +87,20 @@ __device__ __forceinline__ uint4 quant16_f32(const float (&x)[16], float s, floa
 
 // Per-group maximum of |x| over 16 elements per lane and LPV lanes; for float
 // sources a non-finite element makes the result NaN or +inf.
-template <typename Src, int LPV>
-__device__ __forceinline__ typename AccOf<Src>::type group_absmax(const typename AccOf<Src>::type (&x)[16],
+template <typename Src, int LPV, int H = 1>
+__device__ __forceinline__ typename AccOf<Src>::type group_absmax(const typename AccOf<Src>::type (&x)[H][16],
                                                                   int& bad) {
     using Acc = typename AccOf<Src>::type;
     Acc m = Acc(0);
     if constexpr (std::is_same<Src, double>::value) {
         int b = 0;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            b |= !isfinite(x[i]);
-            m = fmax(m, fabs(x[i]));
+        for (int h = 0; h < H; ++h) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                b |= !isfinite(x[h][i]);
+                m = fmax(m, fabs(x[h][i]));
+            }
         }
 #pragma unroll
         for (int off = LPV / 2; off > 0; off >>= 1) {
@@ -107,7 +110,10 @@ __device__ __forceinline__ typename AccOf<Src>::type group_absmax(const typename
         bad = b;
     } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) m = max_nan(m, fabsf(x[i]));
+        for (int h = 0; h < H; ++h) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) m = max_nan(m, fabsf(x[h][i]));
+        }
 #pragma unroll
         for (int off = LPV / 2; off > 0; off >>= 1) m = max_nan(m, __shfl_xor_sync(kFullMask, m, off));
         bad = !(m < INFINITY);
@@ -132,7 +138,9 @@ struct AppendArgs {
     int32_t* status;
 };
 
-template <typename Src, int LPV>
+// H 16-element halves per lane: lane j of a group owns elements
+// [16 H j, 16 H (j + 1)) of its head vector.
+template <typename Src, int LPV, int H>
 __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
     using Acc = typename AccOf<Src>::type;
     if (blockIdx.x >= a.vector_blocks) {  // the trailing block applies table edits
@@ -154,19 +162,23 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
         kv = r & 1;
         a.div_layers.divmod(r >> 1, token, layer_rel);
     }
-    const bool has_chunk = active && (sub * 16 < D);
+    const bool has_chunk = active && (sub * 16 * H < D);
 
-    Acc x[16];
+    Acc x[H][16];
     if (has_chunk) {
         const Src* base = static_cast<const Src*>(kv ? a.values : a.keys) + token * a.s_tok +
-                          layer_rel * a.s_layer + head * a.s_head + sub * 16;
-        load16(base, x);
+                          layer_rel * a.s_layer + head * a.s_head + sub * 16 * H;
+#pragma unroll
+        for (int h = 0; h < H; ++h) load16(base + 16 * h, x[h]);
     } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) x[i] = Acc(0);
+        for (int h = 0; h < H; ++h) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) x[h][i] = Acc(0);
+        }
     }
     int bad = 0;
-    const Acc m = group_absmax<Src, LPV>(x, bad);
+    const Acc m = group_absmax<Src, LPV, H>(x, bad);
     if (!active) return;
 
     const int64_t slot = __ldg(a.slots + token);
@@ -187,7 +199,9 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
                        layer * a.pool.sls + head * a.pool.shs + off;
 
     float s = 0.0f;
-    uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+    uint4 packed[H];
+#pragma unroll
+    for (int h = 0; h < H; ++h) packed[h] = make_uint4(0u, 0u, 0u, 0u);
     if (m != Acc(0)) {
         if constexpr (std::is_same<Src, double>::value) {
             s = scale_from_max(m);
@@ -202,22 +216,28 @@ __global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
             return;
         }
         const float rcp = 1.0f / s;
-        if (!std::is_same<Src, double>::value && s >= kFloatPathMinScale) {
-            float xf[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) xf[i] = static_cast<float>(x[i]);
-            packed = quant16_f32(xf, s, rcp);
-        } else {
-            int q[16];
+        for (int h = 0; h < H; ++h) {
+            if (!std::is_same<Src, double>::value && s >= kFloatPathMinScale) {
+                float xf[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) q[i] = quant_one<Src>(x[i], s, rcp);
-            packed.x = pack4(q[0], q[1], q[2], q[3]);
-            packed.y = pack4(q[4], q[5], q[6], q[7]);
-            packed.z = pack4(q[8], q[9], q[10], q[11]);
-            packed.w = pack4(q[12], q[13], q[14], q[15]);
+                for (int i = 0; i < 16; ++i) xf[i] = static_cast<float>(x[h][i]);
+                packed[h] = quant16_f32(xf, s, rcp);
+            } else {
+                int q[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) q[i] = quant_one<Src>(x[h][i], s, rcp);
+                packed[h].x = pack4(q[0], q[1], q[2], q[3]);
+                packed[h].y = pack4(q[4], q[5], q[6], q[7]);
+                packed[h].z = pack4(q[8], q[9], q[10], q[11]);
+                packed[h].w = pack4(q[12], q[13], q[14], q[15]);
+            }
         }
     }
-    if (has_chunk) *reinterpret_cast<uint4*>(codes + sub * 16) = packed;
+    if (has_chunk) {
+#pragma unroll
+        for (int h = 0; h < H; ++h) *reinterpret_cast<uint4*>(codes + sub * 16 * H + 16 * h) = packed[h];
+    }
     if (sub == 0) *scale_dst = s;
 }
 
@@ -418,16 +438,30 @@ __global__ void __launch_bounds__(256) gather_dequantize_kernel(GatherArgs a) {
 constexpr int kThreads = 256;
 
 template <typename Src>
-sdc_status_t launch_append(int lpv, int64_t blocks, cudaStream_t stream, const AppendArgs& a) {
-    switch (lpv) {
-        case 1: quantize_append_kernel<Src, 1><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 2: quantize_append_kernel<Src, 2><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 4: quantize_append_kernel<Src, 4><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 8: quantize_append_kernel<Src, 8><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 16: quantize_append_kernel<Src, 16><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 32: quantize_append_kernel<Src, 32><<<blocks, kThreads, 0, stream>>>(a); break;
-        default: return SDC_STATUS_UNSUPPORTED;
+sdc_status_t launch_append(int lpv, int halves, int64_t blocks, cudaStream_t stream, const AppendArgs& a) {
+#define SDC_APPEND_CASE(L, H) \
+    case L: quantize_append_kernel<Src, L, H><<<blocks, kThreads, 0, stream>>>(a); break;
+    if (halves == 2) {
+        switch (lpv) {
+            SDC_APPEND_CASE(1, 2)
+            SDC_APPEND_CASE(2, 2)
+            SDC_APPEND_CASE(4, 2)
+            SDC_APPEND_CASE(8, 2)
+            SDC_APPEND_CASE(16, 2)
+            default: return SDC_STATUS_UNSUPPORTED;
+        }
+    } else {
+        switch (lpv) {
+            SDC_APPEND_CASE(1, 1)
+            SDC_APPEND_CASE(2, 1)
+            SDC_APPEND_CASE(4, 1)
+            SDC_APPEND_CASE(8, 1)
+            SDC_APPEND_CASE(16, 1)
+            SDC_APPEND_CASE(32, 1)
+            default: return SDC_STATUS_UNSUPPORTED;
+        }
     }
+#undef SDC_APPEND_CASE
     return launch_status();
 }
 
@@ -648,7 +682,9 @@ SDC_API sdc_status_t sdc_quantize_append(const sdc_page_pool_t* pool, int64_t la
                 return SDC_STATUS_MISALIGNED;
             }
         }
-        const int lpv = lanes_per_vector(pool->head_dim);
+        // float-valued sources take 32 elements per lane when head_dim allows
+        const int halves = (src_dtype != SDC_DTYPE_F64 && pool->head_dim % 32 == 0) ? 2 : 1;
+        const int lpv = lanes_per_vector(pool->head_dim / halves);
         AppendArgs a;
         a.pool = to_pool(pool);
         a.keys = keys;
@@ -673,10 +709,10 @@ SDC_API sdc_status_t sdc_quantize_append(const sdc_page_pool_t* pool, int64_t la
         const int64_t blocks = nblocks + (has_edits ? 1 : 0);
         cudaStream_t st = as_stream(stream);
         switch (src_dtype) {
-            case SDC_DTYPE_F32: return launch_append<float>(lpv, blocks, st, a);
-            case SDC_DTYPE_BF16: return launch_append<__nv_bfloat16>(lpv, blocks, st, a);
-            case SDC_DTYPE_F16: return launch_append<__half>(lpv, blocks, st, a);
-            case SDC_DTYPE_F64: return launch_append<double>(lpv, blocks, st, a);
+            case SDC_DTYPE_F32: return launch_append<float>(lpv, halves, blocks, st, a);
+            case SDC_DTYPE_BF16: return launch_append<__nv_bfloat16>(lpv, halves, blocks, st, a);
+            case SDC_DTYPE_F16: return launch_append<__half>(lpv, halves, blocks, st, a);
+            case SDC_DTYPE_F64: return launch_append<double>(lpv, halves, blocks, st, a);
             default: return SDC_STATUS_UNSUPPORTED;
         }
     } catch (...) {
