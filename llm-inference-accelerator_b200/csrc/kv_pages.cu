@@ -73,7 +73,8 @@ __device__ __forceinline__ uint4 quant16_f32(const float (&x)[16], float s, floa
         const float2 below = __ffma2_rn(__fadd2_rn(n, neghalf2), negs2, a);  // a - (n - 1/2) s
         n.x += (above.x >= 0.0f ? 1.0f : 0.0f) - (below.x < 0.0f ? 1.0f : 0.0f);
         n.y += (above.y >= 0.0f ? 1.0f : 0.0f) - (below.y < 0.0f ? 1.0f : 0.0f);
-        const float2 q = make_float2(copysignf(fminf(n.x, 127.0f), x[i]), copysignf(fminf(n.y, 127.0f), x[i + 1]));
+        // |x| <= m and s = fl(m / 127) give |x| / s < 127.5, so n <= 127 needs no clamp
+        const float2 q = make_float2(copysignf(n.x, x[i]), copysignf(n.y, x[i + 1]));
         const float2 t = __fadd2_rn(q, m2);
         bits[i] = __float_as_uint(t.x);
         bits[i + 1] = __float_as_uint(t.y);
@@ -140,8 +141,10 @@ struct AppendArgs {
 
 // H 16-element halves per lane: lane j of a group owns elements
 // [16 H j, 16 H (j + 1)) of its head vector.
+// Four blocks per SM (at most 64 registers a thread): more loads in flight
+// per SM measured 13 % faster than three blocks at 74 registers.
 template <typename Src, int LPV, int H>
-__global__ void __launch_bounds__(256) quantize_append_kernel(AppendArgs a) {
+__global__ void __launch_bounds__(256, 4) quantize_append_kernel(AppendArgs a) {
     using Acc = typename AccOf<Src>::type;
     if (blockIdx.x >= a.vector_blocks) {  // the trailing block applies table edits
         apply_table_edits(a.edits, threadIdx.x, blockDim.x, a.status);
@@ -300,48 +303,53 @@ __global__ void dequantize_vector_kernel(const int8_t* codes, int64_t count, dou
 struct RollbackArgs {
     Pool pool;
     const int64_t* slots;
-    uint32_t total_vectors;
-    uint32_t vector_blocks;
-    FastDiv div_heads;
+    uint32_t total_rows;  // cleared slots x layers: one warp each
+    uint32_t row_blocks;
+    uint32_t chunks;      // 16-byte code chunks of one slot and layer: 2 x heads x head_dim / 16
     FastDiv div_layers;
     FastDiv div_block;
+    FastDiv div_chunks;   // chunks per head vector: head_dim / 16
     TableEdits edits;
     int32_t* status;
 };
 
-template <int LPV>
+// One warp clears one (slot, layer): the key and value codes of every head,
+// 16-byte chunks spread over the lanes (a head vector's chunks are
+// contiguous, so eight lanes fill one 128-byte row at head_dim 128), and the
+// slot's 2 x heads scales.  The slot's address arithmetic is done once per
+// warp rather than once per chunk.
 __global__ void __launch_bounds__(256) rollback_kernel(RollbackArgs a) {
-    if (blockIdx.x >= a.vector_blocks) {
+    if (blockIdx.x >= a.row_blocks) {
         apply_table_edits(a.edits, threadIdx.x, blockDim.x, a.status);
         return;
     }
-    constexpr int VPW = 32 / LPV;
     const uint32_t lane = threadIdx.x & 31;
-    const uint32_t sub = lane & (LPV - 1);
-    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const uint32_t v = warp * VPW + lane / LPV;
-    if (v >= a.total_vectors) return;
-    const uint32_t D = static_cast<uint32_t>(a.pool.head_dim);
-    uint32_t r, head, index, layer;
-    a.div_heads.divmod(v, r, head);
-    const uint32_t kv = r & 1;
-    a.div_layers.divmod(r >> 1, index, layer);
+    const uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (w >= a.total_rows) return;
+    uint32_t index, layer;
+    a.div_layers.divmod(w, index, layer);
     const int64_t slot = __ldg(a.slots + index);
     if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
-        if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
+        if (lane == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
         return;
     }
     uint32_t blk, off;
     a.div_block.divmod(static_cast<uint32_t>(slot), blk, off);
-    if (sub * 16 < D) {
-        int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
-                        head * a.pool.chs + off * D + sub * 16;
+    const uint32_t H = static_cast<uint32_t>(a.pool.num_heads);
+    const int64_t code_off = blk * a.pool.cbs + layer * a.pool.cls + off * a.pool.head_dim;
+    for (uint32_t c = lane; c < a.chunks; c += 32) {
+        uint32_t row, ch;  // row: kv * H + head
+        a.div_chunks.divmod(c, row, ch);
+        const bool value_side = row >= H;
+        const uint32_t head = value_side ? row - H : row;
+        int8_t* codes = (value_side ? a.pool.values : a.pool.keys) + code_off + head * a.pool.chs + ch * 16;
         *reinterpret_cast<uint4*>(codes) = make_uint4(0u, 0u, 0u, 0u);
     }
-    if (sub == 0) {
-        float* sc = (kv ? a.pool.value_scales : a.pool.key_scales) + blk * a.pool.sbs +
-                    layer * a.pool.sls + head * a.pool.shs + off;
-        *sc = 0.0f;
+    const int64_t scale_off = blk * a.pool.sbs + layer * a.pool.sls + off;
+    for (uint32_t r = lane; r < 2 * H; r += 32) {
+        const bool value_side = r >= H;
+        const uint32_t head = value_side ? r - H : r;
+        (value_side ? a.pool.value_scales : a.pool.key_scales)[scale_off + head * a.pool.shs] = 0.0f;
     }
 }
 
@@ -479,16 +487,8 @@ sdc_status_t launch_gather(int lpv, int64_t blocks, cudaStream_t stream, const G
     return launch_status();
 }
 
-sdc_status_t launch_rollback(int lpv, int64_t blocks, cudaStream_t stream, const RollbackArgs& a) {
-    switch (lpv) {
-        case 1: rollback_kernel<1><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 2: rollback_kernel<2><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 4: rollback_kernel<4><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 8: rollback_kernel<8><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 16: rollback_kernel<16><<<blocks, kThreads, 0, stream>>>(a); break;
-        case 32: rollback_kernel<32><<<blocks, kThreads, 0, stream>>>(a); break;
-        default: return SDC_STATUS_UNSUPPORTED;
-    }
+sdc_status_t launch_rollback(int64_t blocks, cudaStream_t stream, const RollbackArgs& a) {
+    rollback_kernel<<<blocks, kThreads, 0, stream>>>(a);
     return launch_status();
 }
 
@@ -733,23 +733,24 @@ SDC_API sdc_status_t sdc_rollback(const sdc_page_pool_t* pool, const int64_t* cl
         if (num_clear > 0 && clear_slots == nullptr) return SDC_STATUS_NULL_ARGUMENT;
         const bool has_edits = te.num_entries > 0 || te.num_lengths > 0;
         if (num_clear == 0 && !has_edits) return SDC_STATUS_OK;
-        const int lpv = lanes_per_vector(pool->head_dim);
         RollbackArgs a;
         a.pool = to_pool(pool);
         a.slots = clear_slots;
-        const int64_t vectors = num_clear * pool->num_layers * 2 * pool->num_heads;
-        const int64_t nblocks = vector_blocks(vectors, lpv);
-        if (vectors >= INT32_MAX || nblocks + 1 >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        const int64_t rows = num_clear * pool->num_layers;  // one warp per (slot, layer)
+        const int64_t nblocks = ceil_div(rows, kThreads / 32);
+        const int64_t chunks = 2 * pool->num_heads * (pool->head_dim / 16);
+        if (rows >= INT32_MAX || nblocks + 1 >= INT32_MAX || chunks >= INT32_MAX) return SDC_STATUS_OVERFLOW;
         if (pool->num_blocks * pool->block_size >= INT32_MAX) return SDC_STATUS_OVERFLOW;
-        a.total_vectors = static_cast<uint32_t>(vectors);
-        a.vector_blocks = static_cast<uint32_t>(nblocks);
-        a.div_heads = FastDiv(static_cast<uint32_t>(pool->num_heads));
+        a.total_rows = static_cast<uint32_t>(rows);
+        a.row_blocks = static_cast<uint32_t>(nblocks);
+        a.chunks = static_cast<uint32_t>(chunks);
         a.div_layers = FastDiv(static_cast<uint32_t>(pool->num_layers));
         a.div_block = FastDiv(static_cast<uint32_t>(pool->block_size));
+        a.div_chunks = FastDiv(static_cast<uint32_t>(pool->head_dim / 16));
         a.edits = te;
         a.status = device_status;
         const int64_t blocks = nblocks + (has_edits ? 1 : 0);
-        return launch_rollback(lpv, blocks, as_stream(stream), a);
+        return launch_rollback(blocks, as_stream(stream), a);
     } catch (...) {
         return SDC_STATUS_INTERNAL_ERROR;
     }
