@@ -860,12 +860,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (have_prev && !epilogue(prev_own, vf_prev, o_acc)) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(qEmpty + qb));
-            // this group's row sums over all its tokens
+            // this group's row sums over all its tokens: a transposing
+            // reduction (each exchange halves the rows a lane carries) leaves
+            // row `lane`'s warp sum in lane `lane`
             float* red_x = red + (xc & 1) * 4 * RS;
+            {
+                float x[32];
 #pragma unroll
-            for (int r = 0; r < RB; ++r) {
-                const float ws = warp_sum((r & 1) ? l_thr[r / 2].y : l_thr[r / 2].x);
-                if (lane == 0) red_x[qw * RS + r] = ws;
+                for (int r = 0; r < 32; ++r) x[r] = r < RB ? ((r & 1) ? l_thr[r / 2].y : l_thr[r / 2].x) : 0.0f;
+#pragma unroll
+                for (int w = 16; w >= 1; w >>= 1) {
+                    const bool upper = (lane & w) != 0;
+#pragma unroll
+                    for (int i = 0; i < w; ++i) {
+                        const float send = upper ? x[i] : x[i + w];
+                        const float keep = upper ? x[i + w] : x[i];
+                        x[i] = keep + __shfl_xor_sync(kFullMask, send, w);
+                    }
+                }
+                if (lane < RB) red_x[qw * RS + lane] = x[0];
             }
             if (!exchange()) break;
             ++xc;
@@ -873,8 +886,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane < RB) {
                 l_lane = red_x[lane] + red_x[RS + lane] + red_x[2 * RS + lane] + red_x[3 * RS + lane];
             }
-            // merge the two groups' states: group 1 hands its state to group 0
-            if (grp == 1) {
+            // merge the two groups' states: the group that took the item's last
+            // tile finishes it last, so it receives the other group's state,
+            // which moves on to the next item at once
+            const int receiver = static_cast<int>((g - 1) & 1);
+            if (grp != receiver) {
                 if (!warp_wait(bar(mergeEmpty), (merges & 1) ^ 1, abort_flag, a.status)) break;
 #pragma unroll
                 for (int r = 0; r < RB; r += 2) *reinterpret_cast<float2*>(merge_o + tid * RB + r) = o_acc[r / 2];
@@ -938,13 +954,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // apart, 8-row groups 1024 bytes apart), and its factor s1 / 254 * qk_scale.
 // Rows past `rows`, and the padding rows of the MMA's N, are zero.
 template <int RB>
-__global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
+__global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
     using LY = Rows<RB>;
     const AttnArgs& a = t.a;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the item kernel may start its set-up
     if (blockIdx.x > 0) {
         const int lane = threadIdx.x & 31;
-        const int64_t w = static_cast<int64_t>(blockIdx.x - 1) * 32 + (threadIdx.x >> 5);
+        const int64_t w = static_cast<int64_t>(blockIdx.x - 1) * (blockDim.x >> 5) + (threadIdx.x >> 5);
         const int64_t image = w / RB;  // (sequence, KV head, split)
         const int r = static_cast<int>(w - image * RB);
         if (image >= a.batch * a.kv_heads * t.splits) return;
@@ -1018,13 +1034,35 @@ __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
         return static_cast<int>((min(T, (c + 1) * a.chunk) - c * a.chunk + kTile - 1) / kTile);
     };
     const int per_chunk = static_cast<int>(a.kv_heads) * t.splits;
-    for (int64_t b = threadIdx.x; b < a.batch; b += blockDim.x) {
-        const int64_t T = __ldg(a.context_lens + b);
+    // one thread per (sequence, chunk); the trip count is uniform across the
+    // block so every lane takes part in the warp-aggregated position counts
+    const int lane = threadIdx.x & 31;
+    const int64_t pairs = a.batch * a.max_chunks;
+    const int64_t span = (pairs + blockDim.x - 1) / blockDim.x * blockDim.x;
+    auto chunk_tiles = [&](int64_t i, int64_t& b, int64_t& c, int64_t& T) -> int {
+        if (i >= pairs) return -1;
+        b = i / a.max_chunks;
+        c = i - b * a.max_chunks;
+        T = __ldg(a.context_lens + b);
         if (!valid_len(T)) {
-            report_fault(a.status, SDC_FAULT_CONTEXT_RANGE);
-            continue;
+            if (c == 0) report_fault(a.status, SDC_FAULT_CONTEXT_RANGE);
+            return -1;
         }
-        for (int64_t c = 0; c * a.chunk < T; ++c) atomicAdd(&hist[tiles_of(T, c)], per_chunk);
+        return c * a.chunk < T ? tiles_of(T, c) : -1;
+    };
+    // adds `amount` to bin `key` (>= 0) for every lane of the warp that
+    // shares it with one atomic, returning this lane's own start position
+    auto add_to_bin = [&](int key, int32_t amount) -> int32_t {
+        const unsigned peers = __match_any_sync(kFullMask, key);
+        const int leader = __ffs(peers) - 1;
+        int32_t base = 0;
+        if (key >= 0 && lane == leader) base = atomicAdd(&hist[key], amount * __popc(peers));
+        base = __shfl_sync(kFullMask, base, leader);
+        return base + __popc(peers & ((1u << lane) - 1u)) * amount;
+    };
+    for (int64_t i = threadIdx.x; i < span; i += blockDim.x) {
+        int64_t b = 0, c = 0, T = 0;
+        add_to_bin(chunk_tiles(i, b, c, T), per_chunk);
     }
     __syncthreads();
     if (threadIdx.x == 0) {  // bin start positions, largest size first
@@ -1037,25 +1075,23 @@ __global__ void __launch_bounds__(1024) prep_kernel(TcArgs t, int32_t* first) {
         *const_cast<int32_t*>(t.item_count) = running;
     }
     __syncthreads();
-    for (int64_t b = threadIdx.x; b < a.batch; b += blockDim.x) {
-        const int64_t T = __ldg(a.context_lens + b);
-        if (!valid_len(T)) continue;
-        for (int64_t c = 0; c * a.chunk < T; ++c) {
-            const int tiles = tiles_of(T, c);
-            for (int64_t h = 0; h < a.kv_heads; ++h) {
-                const int32_t pos = atomicAdd(&hist[tiles], t.splits);
-                for (int sp = 0; sp < t.splits; ++sp) {
-                    WorkItem w;
-                    w.b = static_cast<int32_t>(b);
-                    w.h = static_cast<int32_t>(h);
-                    w.t0 = static_cast<int32_t>(c * a.chunk);
-                    w.t1 = static_cast<int32_t>(min(T, (c + 1) * a.chunk));
-                    w.ctx = static_cast<int32_t>(T);
-                    w.chunk = static_cast<int32_t>(c);
-                    w.split = sp;
-                    w.pad = 0;
-                    const_cast<WorkItem*>(t.items)[pos + sp] = w;
-                }
+    for (int64_t i = threadIdx.x; i < span; i += blockDim.x) {
+        int64_t b = 0, c = 0, T = 0;
+        const int tiles = chunk_tiles(i, b, c, T);
+        const int32_t pos = add_to_bin(tiles, per_chunk);
+        if (tiles < 0) continue;
+        for (int64_t h = 0; h < a.kv_heads; ++h) {
+            for (int sp = 0; sp < t.splits; ++sp) {
+                WorkItem w;
+                w.b = static_cast<int32_t>(b);
+                w.h = static_cast<int32_t>(h);
+                w.t0 = static_cast<int32_t>(c * a.chunk);
+                w.t1 = static_cast<int32_t>(min(T, (c + 1) * a.chunk));
+                w.ctx = static_cast<int32_t>(T);
+                w.chunk = static_cast<int32_t>(c);
+                w.split = sp;
+                w.pad = 0;
+                const_cast<WorkItem*>(t.items)[pos + h * t.splits + sp] = w;
             }
         }
     }
@@ -1153,7 +1189,7 @@ sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUten
                            const CUtensorMap& ksmap, const CUtensorMap& vsmap, int32_t* first, cudaStream_t st) {
     using LY = Rows<RB>;
     const int64_t query_warps = t.a.batch * t.a.kv_heads * t.splits * RB;
-    prep_kernel<RB><<<static_cast<unsigned>(1 + (query_warps + 31) / 32), 1024, 0, st>>>(t, first);
+    prep_kernel<RB><<<static_cast<unsigned>(1 + (query_warps + 7) / 8), 256, 0, st>>>(t, first);
     auto kernel = attn_tc_kernel<RB>;
     static bool configured = false;
     if (!configured) {
