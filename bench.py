@@ -42,6 +42,12 @@ VERIFY = dict(batch=32, query_heads=32, kv_heads=8, head_dim=128, window=5, bloc
               min_context=1024, max_context=8192)
 APPEND = dict(layers=32, kv_heads=8, head_dim=128, sequences=256, window=5, block_size=16, num_blocks=65536)
 LONG = dict(batch=8, query_heads=64, kv_heads=8, head_dim=128, window=5, block_size=16, context=131072)
+# end-to-end speculative decoding: random-init Llama-architecture draft and
+# target (bf16, weights N(0, 0.02)), uniform random prompt ids
+SPEC = dict(batch=64, prompt=1024, new_tokens=64, window=5, min_window=4, max_window=8, temperature=1.0,
+            vocab=128256,
+            draft=dict(layers=16, hidden=2048, heads=32, kv_heads=8, head_dim=64, intermediate=8192),
+            target=dict(layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128, intermediate=14336))
 FLUSH_BYTES = 256 << 20
 HOLD_CYCLES = 200_000  # about 0.1 ms of device time at B200 clocks
 
@@ -66,6 +72,8 @@ def parse_args(argv=None):
     p.add_argument("--skip-append", action="store_true", help="measure only the verify attention")
     p.add_argument("--skip-cpu-baseline", action="store_true")
     p.add_argument("--skip-long", action="store_true", help="skip the 70B long-context (KV-head parallel) workload")
+    p.add_argument("--skip-speculative", action="store_true",
+                   help="skip the end-to-end speculative decoding workload (draft 16L d2048 / target 32L d4096)")
     p.add_argument("--profile-append", action="store_true",
                    help="the append workload's step (256 sequences x 5 tokens, 32 layers) on a 4096-block pool, "
                         "a few steps, no timing: small enough for a full ncu capture")
@@ -343,6 +351,106 @@ def time_verify_e2e(state, steps: int, warmup: int, world: int, flush):
     barrier(world)
     return start.elapsed_time(end), q_host[0].numel() * q_host[0].element_size(), \
         out_host[0].numel() * out_host[0].element_size()
+
+
+# ---------------------------------------------------------------------------
+# end-to-end speculative decoding
+# ---------------------------------------------------------------------------
+
+def _random_llama(spec: dict, vocab: int, device):
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    config = LlamaConfig(hidden_size=spec["hidden"], intermediate_size=spec["intermediate"],
+                         num_hidden_layers=spec["layers"], num_attention_heads=spec["heads"],
+                         num_key_value_heads=spec["kv_heads"], head_dim=spec["head_dim"], vocab_size=vocab,
+                         max_position_embeddings=8192, initializer_range=0.02)
+    previous = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(device):
+            model = LlamaForCausalLM(config)
+    finally:
+        torch.set_default_dtype(previous)
+    return model.eval()
+
+
+def run_speculative(seed: int, device, world: int):
+    """Batched speculative decoding through the paged caches: prefill the
+    prompts, then time the decoding rounds (draft proposals, target verify,
+    device-side acceptance, rollback) on the device; the attention calls of
+    both models are timed individually."""
+    import numpy as np
+    import torch
+
+    from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
+    from specdecode_b200.speculative import BatchedSpeculativeDecoder, DraftWindow
+
+    sp = SPEC
+    torch.manual_seed(seed)
+    draft = _random_llama(sp["draft"], sp["vocab"], device)
+    target = _random_llama(sp["target"], sp["vocab"], device)
+    B = sp["batch"]
+    tokens = sp["prompt"] + 2 * sp["new_tokens"] + 2 * sp["max_window"]
+    blocks = B * (-(-tokens // 16) + 1)
+
+    def cache(spec):
+        return PagedKVCache(KVCacheConfig(spec["layers"], spec["kv_heads"], spec["head_dim"], block_size=16,
+                                          num_blocks=blocks), device=device, max_sequences=B, check_status=False)
+
+    dec = BatchedSpeculativeDecoder(draft, target, cache(sp["draft"]), cache(sp["target"]),
+                                    window=DraftWindow(sp["window"], sp["min_window"], sp["max_window"]),
+                                    temperature=sp["temperature"], seed=seed)
+    rng = np.random.default_rng(seed)
+    prompts = torch.from_numpy(rng.integers(0, sp["vocab"], size=(B, sp["prompt"]), dtype=np.int64)).to(device)
+    with torch.no_grad():
+        dec.generate(prompts, 8)  # warm-up: kernels, workspaces, allocator
+        dec.window.size = sp["window"]
+        for session in (dec.draft, dec.target):
+            session.timed = True
+            session.timings.clear()
+        start, prefilled, end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        result = dec.generate(prompts, sp["new_tokens"], prefill_done=prefilled)
+        end.record()
+        torch.cuda.synchronize()
+    prefill_ms = start.elapsed_time(prefilled)
+    decode_ms = prefilled.elapsed_time(end)
+    attn = {}
+    for name, session in (("draft", dec.draft), ("target", dec.target)):
+        ms, nbytes = session.attention_time()
+        attn[name] = (ms, nbytes, len(session.timings))
+        session.timed = False
+    peak, peak_kind = measured_peaks()
+    tokens_out = B * sp["new_tokens"]
+    decode_max = max_over_ranks(decode_ms, world)
+    attn_ms = sum(v[0] for v in attn.values())
+    attn_bytes = sum(v[1] for v in attn.values())
+    stats = result.stats
+    out = {
+        "config": f"draft Llama 16L d2048 32/8 heads D64, target Llama 32L d4096 32/8 heads D128, vocab "
+                  f"{sp['vocab']}, random-init bf16 N(0, 0.02); batch {B} x prompt {sp['prompt']} uniform ids, "
+                  f"{sp['new_tokens']} new tokens each, window {sp['min_window']}-{sp['max_window']} (start "
+                  f"{sp['window']}), temperature {sp['temperature']}; both models attend over INT8 pages",
+        "parallelism": f"request data-parallel x{world}, a full model pair per GPU",
+        "tokens_per_s": sum_over_ranks(tokens_out, world) / (decode_max / 1e3),
+        "tokens_per_s_with_prefill": sum_over_ranks(tokens_out, world) / (max_over_ranks(prefill_ms + decode_ms, world) / 1e3),
+        "decode_ms": decode_max,
+        "prefill_ms": max_over_ranks(prefill_ms, world),
+        "acceptance_rate": stats.acceptance_rate,
+        "verification_rounds": stats.verification_rounds,
+        "attention_ms": attn_ms,
+        "attention_share_of_run": attn_ms / (prefill_ms + decode_ms),
+        "attention_gbs": attn_bytes / (attn_ms / 1e3) / 1e9 if attn_ms > 0 else None,
+        "attention_fraction_of_peak": attn_bytes / (attn_ms / 1e3) / 1e9 / peak if attn_ms > 0 else None,
+        "attention_calls": {k: v[2] for k, v in attn.items()},
+        "peak_source": peak_kind,
+    }
+    del dec, draft, target
+    torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -672,6 +780,10 @@ def main(argv=None) -> int:
     if not args.skip_long:
         long_ctx = run_long_context(args.seed, rank, world, device, args.steps, args.warmup)
 
+    speculative = None
+    if not args.skip_speculative:
+        speculative = run_speculative(args.seed + 1000 * rank, device, world)
+
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         cpu = cpu_attention_baseline(state)
@@ -707,6 +819,7 @@ def main(argv=None) -> int:
             "gpu_launches": 3 * args.steps,
             "append": append,
             "long_context_70b": long_ctx,
+            "speculative_e2e": speculative,
             "cpu_baseline": cpu,
             "clocks": clocks,
         }

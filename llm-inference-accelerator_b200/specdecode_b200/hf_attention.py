@@ -75,6 +75,10 @@ class PagedAttentionSession:
         self._ids: list[Hashable] = []
         self._new = 0
         self._inputs = None
+        # optional device timing of the attention calls: (start, end, algorithmic bytes)
+        self.timed = False
+        self.timings: list = []
+        self._lengths: list[int] = []
         register()
 
     @contextlib.contextmanager
@@ -87,6 +91,8 @@ class PagedAttentionSession:
         self._new = int(new_tokens)
         self._pending = self.cache.reserve(self._ids, self._new)
         self._inputs = self.cache.attention_inputs(self._ids)
+        if self.timed:
+            self._lengths = [self.cache.sequence_length(s) for s in self._ids]
         _ACTIVE.append(self)
         try:
             yield self
@@ -117,13 +123,38 @@ class PagedAttentionSession:
         group = Hq // Hkv
         window = max(1, _MAX_ROWS // group)
         if q_len <= window:
-            out = self.attention(query.contiguous(), tables, lens, max_len, layer)
+            out = self._attend(query.contiguous(), tables, lens, max_len, layer, 0)
         else:
             parts = []
             for j in range(0, q_len, window):
                 w = min(window, q_len - j)
                 behind = q_len - (j + w)  # new tokens after this window
-                parts.append(self.attention(query[:, :, j:j + w].contiguous(), tables, lens - behind,
-                                            max_len - behind, layer))
+                parts.append(self._attend(query[:, :, j:j + w].contiguous(), tables, lens - behind,
+                                          max_len - behind, layer, behind))
             out = torch.cat(parts, dim=2)
         return out.transpose(1, 2).contiguous(), None
+
+    def _attend(self, query, tables, lens, max_len, layer, behind):
+        if not self.timed:
+            return self.attention(query, tables, lens, max_len, layer)
+        import torch
+
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        out = self.attention(query, tables, lens, max_len, layer)
+        end.record()
+        B, Hq, w, D = (int(d) for d in query.shape)
+        cfg = self.cache.config
+        per_token = 2 * cfg.num_heads * D + 2 * cfg.num_heads * 4
+        nbytes = sum((t - behind) * per_token + -(-(t - behind) // cfg.block_size) * 4 for t in self._lengths)
+        nbytes += 2 * B * Hq * w * D * query.element_size()
+        self.timings.append((start, end, nbytes))
+        return out
+
+    def attention_time(self) -> tuple[float, int]:
+        """Milliseconds and algorithmic bytes of the timed attention calls so
+        far (synchronises the device)."""
+        import torch
+
+        torch.cuda.synchronize()
+        return sum(s.elapsed_time(e) for s, e, _ in self.timings), sum(b for _, _, b in self.timings)

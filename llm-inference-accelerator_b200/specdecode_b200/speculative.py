@@ -1,0 +1,262 @@
+"""Batched speculative decoding over the paged INT8 caches.
+
+The reference decoder (src/specdecode/decoder.py:69-257, ``SpeculativeDecoder``)
+runs one sequence at a time: the draft proposes up to a window of tokens,
+the target scores them, each proposal is accepted with probability
+``min(1, p_target / p_draft)`` (src/specdecode/backends.py, native
+``sd_acceptance_probabilities_f64``), the first rejected position is
+resampled from the normalised residual ``max(0, p_target - p_draft)`` and a
+fully accepted window earns one bonus token from the target.  Its models
+rebuild a legacy cache from the paged mirror on every forward
+(src/specdecode/huggingface.py:382-393).
+
+``BatchedSpeculativeDecoder`` runs the same rule for a whole batch with both
+models reading and writing their own device page pools through the
+attention hook (``hf_attention``): kernel (a) appends each layer's new keys
+and values, kernel (c) attends over the pool, kernel (b) rolls back the
+rejected tail, and sampling stays on the device (one device-to-host read of
+the round's accepted counts and tokens per round).
+
+Cache convention: every committed token but the last is in both caches.  A
+round feeds the draft ``last, d_1 .. d_k`` one token at a time (sampling
+``d_i`` from the draft's distribution after ``d_{i-1}``), feeds the target
+the same ``k + 1`` tokens in one verify pass, and, with ``j`` proposals
+accepted, truncates both caches to the old length plus ``j + 1``.
+
+All sequences of a batch share the round's window; the window adapts
+between rounds with the reference's rule (src/specdecode/decoder.py:47-60)
+applied to the batch's mean acceptance.  Temperature 0 selects greedy
+verification (accept while the draft token is the target's argmax).  No
+end-of-sequence handling: every sequence generates ``max_new_tokens``.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Hashable, Sequence
+
+from .hf_attention import PagedAttentionSession
+from .kv_cache import PagedKVCache
+
+
+@dataclass
+class DecodeStats:
+    """Counters with the meaning of the reference's ``DecodeStats``
+    (src/specdecode/decoder.py:21-34), summed over the batch."""
+
+    drafted_tokens: int = 0
+    accepted_tokens: int = 0
+    rejected_tokens: int = 0
+    target_tokens: int = 0
+    verification_rounds: int = 0
+
+    @property
+    def acceptance_rate(self) -> float:
+        return self.accepted_tokens / self.drafted_tokens if self.drafted_tokens else 0.0
+
+
+@dataclass
+class BatchDecodeResult:
+    prompt_tokens: list[list[int]]
+    generated_tokens: list[list[int]]
+    stats: DecodeStats = field(default_factory=DecodeStats)
+
+
+@dataclass
+class DraftWindow:
+    """The reference's adaptive draft length (src/specdecode/decoder.py:47-60)."""
+
+    size: int = 5
+    min_size: int = 4
+    max_size: int = 8
+    dynamic: bool = True
+
+    def observe(self, accepted: float, proposed: int) -> None:
+        if not self.dynamic or proposed == 0:
+            return
+        if accepted >= proposed:
+            self.size = min(self.max_size, self.size + 1)
+        elif accepted * 2 < proposed:
+            self.size = max(self.min_size, self.size // 2)
+        else:
+            self.size = max(self.min_size, self.size - 1)
+
+
+def _distribution(logits, temperature: float):
+    import torch
+
+    return torch.softmax(logits.float() / temperature, dim=-1)
+
+
+def accept_sampled(drafts, draft_probs, target_probs, generator):
+    """The reference's acceptance rule for a batch of windows.
+
+    ``drafts`` int64 ``[B, k]`` were sampled from ``draft_probs [B, k, V]``;
+    ``target_probs [B, k + 1, V]`` are the target's distributions at the same
+    positions plus the bonus position.  Proposal i is accepted with
+    probability ``min(1, q_i(d_i) / p_i(d_i))`` until the first rejection,
+    which is replaced by a sample of ``max(0, q_j - p_j)`` normalised; a fully
+    accepted window adds a sample of ``q_{k+1}``.  Returns the accepted
+    counts ``[B]`` and the round's final token ``[B, 1]``."""
+    import torch
+
+    B, k = drafts.shape
+    q_d = target_probs[:, :k].gather(2, drafts[:, :, None]).squeeze(2)
+    p_d = draft_probs.gather(2, drafts[:, :, None]).squeeze(2)
+    ratio = torch.where(p_d > 0, q_d / p_d, torch.ones_like(q_d))
+    u = torch.rand((B, k), generator=generator, device=drafts.device)
+    ok = u < torch.clamp(ratio, max=1.0)
+    accepted = torch.cumprod(ok.int(), dim=1).sum(dim=1)
+    idx = accepted[:, None, None].expand(B, 1, target_probs.shape[-1])
+    q_j = target_probs.gather(1, idx).squeeze(1)
+    p_full = torch.cat([draft_probs, torch.zeros_like(draft_probs[:, :1])], dim=1)
+    p_j = p_full.gather(1, idx).squeeze(1)
+    resid = torch.clamp(q_j - p_j, min=0.0)
+    weights = torch.where(resid.sum(dim=-1, keepdim=True) > 0, resid, q_j)
+    return accepted, torch.multinomial(weights, 1, generator=generator)
+
+
+def accept_greedy(drafts, target_logits):
+    """Greedy verification: proposals are accepted while they equal the
+    target's argmax; the final token is the target's argmax after them."""
+    import torch
+
+    k = drafts.shape[1]
+    best = target_logits.argmax(dim=-1)
+    accepted = torch.cumprod((drafts == best[:, :k]).int(), dim=1).sum(dim=1)
+    return accepted, best.gather(1, accepted[:, None])
+
+
+class BatchedSpeculativeDecoder:
+    """Speculative decoding of a batch with a draft and a target transformers
+    causal LM, each attending over its own ``PagedKVCache``.
+
+    ``draft_cache`` / ``target_cache`` must have the models' layer count, KV
+    heads and head_dim and room for every sequence's prompt plus generated
+    tokens plus one window.  Sequences are registered in the caches by the
+    decoder (ids ``(tag, i)``) and removed when ``generate`` returns.
+    """
+
+    def __init__(self, draft_model, target_model, draft_cache: PagedKVCache, target_cache: PagedKVCache, *,
+                 window: DraftWindow | None = None, temperature: float = 1.0, seed: int = 0) -> None:
+        if draft_model.config.vocab_size != target_model.config.vocab_size:
+            raise ValueError("draft and target models must share a vocabulary")
+        if temperature < 0 or not math.isfinite(temperature):
+            raise ValueError("temperature must be finite and non-negative")
+        self.draft_model = draft_model
+        self.target_model = target_model
+        self.draft = PagedAttentionSession(draft_cache)
+        self.target = PagedAttentionSession(target_cache)
+        self.window = window or DraftWindow()
+        self.temperature = float(temperature)
+        self.seed = int(seed)
+        self._tag = 0
+        for model in (draft_model, target_model):
+            model.set_attn_implementation(PagedAttentionSession.NAME)
+
+    # -- model passes ---------------------------------------------------------
+    def _forward(self, session: PagedAttentionSession, model, ids: Sequence[Hashable], tokens, keep: int):
+        """Feeds ``tokens [B, n]`` to ``model`` after each sequence's cached
+        tokens; returns the logits of the last ``keep`` positions."""
+        import torch
+
+        cache = session.cache
+        B, n = tokens.shape
+        lengths = torch.tensor([cache.sequence_length(s) for s in ids], device=tokens.device)
+        positions = lengths[:, None] + torch.arange(n, device=tokens.device)[None, :]
+        with session.step(ids, n):
+            out = model(input_ids=tokens, position_ids=positions, use_cache=False, logits_to_keep=keep)
+        return out.logits
+
+    def _prefill(self, session: PagedAttentionSession, model, ids, tokens, chunk: int) -> None:
+        for i in range(0, tokens.shape[1], chunk):
+            self._forward(session, model, ids, tokens[:, i:i + chunk], 1)
+
+    # -- decoding -------------------------------------------------------------
+    def generate(self, prompt_tokens, max_new_tokens: int, *, prefill_chunk: int = 512,
+                 prefill_done=None) -> BatchDecodeResult:
+        """``prompt_tokens``: int64 ``[B, P]`` (device or host), P >= 1.
+        ``prefill_done``: an optional CUDA event recorded once both caches
+        hold the prompts (before the first round)."""
+        import torch
+
+        device = self.target.cache.device
+        prompts = torch.as_tensor(prompt_tokens, dtype=torch.long).to(device)
+        if prompts.dim() != 2 or prompts.shape[1] < 1:
+            raise ValueError("prompt_tokens must be [batch, prompt_length] with prompt_length >= 1")
+        B = int(prompts.shape[0])
+        self._tag += 1
+        ids = [(self._tag, i) for i in range(B)]
+        gen = torch.Generator(device=device).manual_seed(self.seed)
+        stats = DecodeStats()
+        generated = [[] for _ in range(B)]
+        for cache in (self.draft.cache, self.target.cache):
+            for s in ids:
+                cache.create_sequence(s)
+        try:
+            if prompts.shape[1] > 1:
+                ctx = prompts[:, :-1]
+                self._prefill(self.draft, self.draft_model, ids, ctx, prefill_chunk)
+                self._prefill(self.target, self.target_model, ids, ctx, prefill_chunk)
+            last = prompts[:, -1:]
+            if prefill_done is not None:
+                prefill_done.record()
+            while min(len(g) for g in generated) < max_new_tokens:
+                last = self._round(ids, last, gen, stats, generated)
+        finally:
+            for cache in (self.draft.cache, self.target.cache):
+                for s in ids:
+                    cache.remove_sequence(s)
+        return BatchDecodeResult(prompts.cpu().tolist(), [g[:max_new_tokens] for g in generated], stats)
+
+    def _round(self, ids, last, gen, stats: DecodeStats, generated) -> "torch.Tensor":
+        import torch
+
+        k = self.window.size
+        B = last.shape[0]
+        greedy = self.temperature == 0.0
+        dlen = [self.draft.cache.sequence_length(s) for s in ids]
+        tlen = [self.target.cache.sequence_length(s) for s in ids]
+        # draft: k proposals, one token per pass; d_k is fed too so that a
+        # fully accepted window leaves the draft cache complete
+        feed = last
+        proposals, draft_probs = [], []
+        for i in range(k + 1):
+            logits = self._forward(self.draft, self.draft_model, ids, feed, 1)[:, -1]
+            if i == k:
+                break
+            if greedy:
+                tok = logits.argmax(dim=-1, keepdim=True)
+            else:
+                p = _distribution(logits, self.temperature)
+                tok = torch.multinomial(p, 1, generator=gen)
+                draft_probs.append(p)
+            proposals.append(tok)
+            feed = tok
+        drafts = torch.cat(proposals, dim=1)  # [B, k]
+        # target: one verify pass over last, d_1 .. d_k
+        verify = torch.cat([last, drafts], dim=1)
+        tlogits = self._forward(self.target, self.target_model, ids, verify, k + 1)  # [B, k + 1, V]
+        if greedy:
+            accepted, new_tok = accept_greedy(drafts, tlogits)
+        else:
+            accepted, new_tok = accept_sampled(drafts, torch.stack(draft_probs, dim=1),
+                                               _distribution(tlogits, self.temperature), gen)
+        host = torch.cat([accepted[:, None], drafts, new_tok], dim=1).cpu().tolist()
+        keep_d, keep_t = [], []
+        for b, row in enumerate(host):
+            j = int(row[0])
+            generated[b].extend(row[1:1 + j])
+            generated[b].append(int(row[1 + k]))
+            keep_d.append(dlen[b] + 1 + j)
+            keep_t.append(tlen[b] + 1 + j)
+            stats.accepted_tokens += j
+            stats.rejected_tokens += int(j < k)
+        self.draft.cache.truncate_batch(ids, keep_d)
+        self.target.cache.truncate_batch(ids, keep_t)
+        stats.drafted_tokens += B * k
+        stats.target_tokens += B
+        stats.verification_rounds += 1
+        self.window.observe(sum(int(r[0]) for r in host) / B, k)
+        return new_tok
