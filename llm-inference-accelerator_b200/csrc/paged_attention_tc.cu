@@ -290,12 +290,6 @@ __device__ __forceinline__ float redux_max(float v) {
     return r;
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFullMask, v, off);
-    return v;
-}
-
 __device__ __forceinline__ float fast_exp2(float x) {
     float r;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
