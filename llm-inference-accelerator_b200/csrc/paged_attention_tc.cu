@@ -46,10 +46,7 @@ namespace sdc {
 namespace tc {
 namespace {
 
-constexpr int kTile = 128;     // tokens per tile (MMA M for S^T)
-constexpr int kHeadDim = 128;  // MMA M for O^T, and the K extent of S^T
-constexpr int kCodeTileBytes = kTile * kHeadDim;                 // 16 KiB
-constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;  // K, V codes + scales
+constexpr int kTile = 128;  // tokens per tile (MMA M for S^T)
 constexpr int kGroups = 2;                                       // softmax warpgroups
 constexpr int kKeyWarp = 8;  // key codes of every page
 constexpr int kMmaWarp = 9;
@@ -63,11 +60,19 @@ constexpr int kMaxSplits = 2;
 // Largest work item in tiles (the chunk size is clamped to 16384 tokens).
 constexpr int kMaxItemTiles = 16384 / kTile;
 
-template <int RB>
+// Layout of the kernel for RB query rows per item and head_dim HD (64 or
+// 128): HD is the MMA M of O^T and the K extent of S^T.  A page row is HD
+// bytes; key / value tiles use the 128-byte swizzle at HD 128 and the
+// 64-byte swizzle at HD 64, which is also how TMA writes them.
+template <int RB, int HD>
 struct Rows {
+    static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+    static constexpr int kCodeTileBytes = kTile * HD;                 // one K or V tile
+    static constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;  // K, V codes + scales
+    static constexpr uint32_t kSwizzle = HD == 128 ? 2u : 4u;       // descriptor layout: 128B / 64B swizzle
     static constexpr int N = ((2 * RB + 15) / 16) * 16;  // MMA N
-    static constexpr int kStages = RB <= 24 ? 5 : 4;
-    static constexpr int kQCodes = N * kHeadDim;
+    static constexpr int kStages = HD == 64 ? 8 : (RB <= 24 ? 5 : 4);
+    static constexpr int kQCodes = N * HD;
     // one query image: the codes, then the RB row factors; global images
     // are kQStride bytes apart, shared-memory buffers kQBufBytes
     static constexpr int kQCopyBytes = kQCodes + RB * 4;
@@ -96,9 +101,10 @@ struct Rows {
     static_assert(RB % 4 == 0, "row factors fill whole 16-byte words");
 };
 
-// Bytes between two (sequence, KV head) query images for row bucket rb.
-constexpr int64_t query_image_stride(int rb) {
-    return ((((2 * rb + 15) / 16) * 16 * kHeadDim + rb * 4 + 127) / 128) * 128;
+// Bytes between two (sequence, KV head) query images for row bucket rb and
+// head_dim hd.
+constexpr int64_t query_image_stride(int rb, int hd) {
+    return ((((2 * rb + 15) / 16) * 16 * hd + rb * 4 + 127) / 128) * 128;
 }
 
 // One unit of work: tokens [t0, t1) of sequence b (context length ctx) for
@@ -303,13 +309,15 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t w0, uint32_t w1, uin
 
 // ---------------------------------------------------------------- main kernel
 
-template <int RB>
+template <int RB, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    const __grid_constant__ CUtensorMap ksmap, const __grid_constant__ CUtensorMap vsmap, TcArgs t) {
-    using LY = Rows<RB>;
+    using LY = Rows<RB, HD>;
     constexpr int N = LY::N;
     constexpr int STAGES = LY::kStages;
+    constexpr int kCodeTileBytes = LY::kCodeTileBytes;
+    constexpr int kStageBytes = LY::kStageBytes;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -402,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool scale_side = warp == kScaleWarp;
         const CUtensorMap* map = warp == kKeyWarp ? &kmap : &vmap;
         const uint32_t code_dst = (warp == kKeyWarp ? 0u : static_cast<uint32_t>(kCodeTileBytes)) +
-                                  static_cast<uint32_t>(lane * bs * kHeadDim);
-        const uint32_t code_bytes = static_cast<uint32_t>(bs * kHeadDim);
+                                  static_cast<uint32_t>(lane * bs * HD);
+        const uint32_t code_bytes = static_cast<uint32_t>(bs * HD);
         const uint32_t scale_bytes = static_cast<uint32_t>(bs * 4);
         const int lg_bs = __ffs(static_cast<int>(bs)) - 1;  // block sizes are powers of two
         const bool gather = t.gather4 != 0;
@@ -455,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) mbar_arrive_expect_tx(bar(kvFull + s), __popc(mask) * code_bytes);
                     __syncwarp();
                     if (valid) {
-                        const int32_t row = static_cast<int32_t>((blk * a.pool.cbs + code_base) / kHeadDim);
+                        const int32_t row = static_cast<int32_t>((blk * a.pool.cbs + code_base) / HD);
                         tma_load_2d(st + code_dst, map, 0, row, bar(kvFull + s));
                     }
                 } else if (gather) {
@@ -508,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // behind it.  Both waits are polled; the thread gives up after
         // kWaitLimitCycles without progress.
         constexpr uint32_t kIdescS = idesc_i8(kTile, N, 0, 0);
-        constexpr uint32_t kIdescO = idesc_i8(kHeadDim, N, 1, 1);
+        constexpr uint32_t kIdescO = idesc_i8(HD, N, 1, 1);
         if (lane == 0) {
             uint32_t gs = 0, gp = 0, li = 0;
             int k = 0;
@@ -532,9 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t k_tile = stage_base + s * kStageBytes;
                         const uint32_t q_tile = q_base + qb * LY::kQBufBytes;
 #pragma unroll
-                        for (int ks = 0; ks < kHeadDim / 32; ++ks) {
-                            const uint64_t da = smem_desc(k_tile + ks * 32, 16, 1024, 2);
-                            const uint64_t db = smem_desc(q_tile + ks * 256, 128, 1024, 0);
+                        for (int ks = 0; ks < HD / 32; ++ks) {
+                            const uint64_t da = smem_desc(k_tile + ks * 32, 16, 8 * HD, LY::kSwizzle);
+                            const uint64_t db = smem_desc(q_tile + ks * 256, 128, 8 * HD, 0);
                             mma_i8(tmem + sb * LY::kTmemStride, da, db, kIdescS, ks > 0);
                         }
                         mma_commit(bar(sFull + sb));
@@ -569,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t p_tile = p_base + (sb * 2 + ((gp >> 1) & 1)) * LY::kPBytes;
 #pragma unroll
                         for (int ks = 0; ks < kTile / 32; ++ks) {
-                            const uint64_t da = smem_desc(v_tile + ks * 4096, kCodeTileBytes, 1024, 2);
+                            const uint64_t da = smem_desc(v_tile + ks * 32 * HD, kCodeTileBytes, 8 * HD, LY::kSwizzle);
                             const uint64_t db = smem_desc(p_tile + ks * 512, 128, 2048, 0);
                             mma_i8(tmem + (2 + sb) * LY::kTmemStride, da, db, kIdescO, ks > 0);
                         }
@@ -613,7 +621,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // packed f32x2 arithmetic of sm_100.
         const int grp = warp >> 2;
         const int qw = warp & 3;            // lane quarter = TMEM lanes [32 qw, 32 qw + 32)
-        const int tid = threadIdx.x & 127;  // token row of S^T, head_dim row of O^T
+        const int tid = threadIdx.x & 127;  // token row of S^T
+        // head_dim row of O^T held by this thread: at HD 128 row tid; at HD
+        // 64 (an M = 64 product) rows 16 qw .. 16 qw + 15 sit in lanes 0-15
+        // of each warp's lane quarter and lanes 16-31 hold none
+        const bool o_row = HD == 128 || lane < 16;
+        const int dcol = HD == 128 ? tid : qw * 16 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(qw * 32) << 16;
         const uint32_t s_col = grp * LY::kTmemStride;
         const uint32_t o_col = (2 + grp) * LY::kTmemStride;
@@ -909,14 +922,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
                 const int64_t chunk = it.chunk;
-                float* part_o = a.part_o + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * kHeadDim;
+                float* part_o = a.part_o + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * HD;
                 float* part_ml = a.part_ml + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * 2;
 #pragma unroll
                 for (int r = 0; r < RB; ++r) {
                     const float e0 = __shfl_sync(kFullMask, e0_lane, r);
                     const float e1 = __shfl_sync(kFullMask, e1_lane, r);
                     const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
-                    if (r < R) part_o[r * kHeadDim + tid] = o0 * e0 + merge_o[tid * RB + r] * e1;
+                    if (r < R && o_row) part_o[r * HD + dcol] = o0 * e0 + merge_o[tid * RB + r] * e1;
                 }
                 if (qw == 0 && lane < R) {
                     part_ml[2 * lane + 0] = m_tot;
@@ -945,11 +958,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // rows, one warp per (sequence, KV head, row): each row splits into INT8
 // hi / lo parts written in the score MMA's B layout (K-major, no swizzle:
 // 8 rows x 16 bytes per 128-byte core matrix, 16-byte K chunks 128 bytes
-// apart, 8-row groups 1024 bytes apart), and its factor s1 / 254 * qk_scale.
-// Rows past `rows`, and the padding rows of the MMA's N, are zero.
-template <int RB>
+// apart, 8-row groups 8 x HD bytes apart), and its factor s1 / 254 * qk_scale.
+// Rows past `rows`, and the padding rows of the MMA's N, are zero.  At HD
+// 64 lanes 16-31 of a row's warp hold no elements.
+template <int RB, int HD>
 __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
-    using LY = Rows<RB>;
+    using LY = Rows<RB, HD>;
     const AttnArgs& a = t.a;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the item kernel may start its set-up
     if (blockIdx.x > 0) {
@@ -964,9 +978,10 @@ __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
         const int64_t h = bh - b * a.kv_heads;
         unsigned char* img = t.qimg + image * LY::kQStride;
         const int d = lane * 4;
+        const bool has_d = d < HD;
         float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (r < t.rows && row < t.total_rows) {
-            const int64_t e = ((b * a.query_heads + h * a.group) * a.window + row) * kHeadDim + d;
+        if (has_d && r < t.rows && row < t.total_rows) {
+            const int64_t e = ((b * a.query_heads + h * a.group) * a.window + row) * HD + d;
             if (a.query_dtype == SDC_DTYPE_BF16) {
                 const uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.query) + e));
                 x[0] = __uint_as_float(v.x << 16);
@@ -1006,10 +1021,12 @@ __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
             }
             factor = s1 / 254.0f * a.qk_scale;
         }
-        auto offset = [&](int n) { return (n >> 3) * 1024 + (d >> 4) * 128 + (n & 7) * 16 + (d & 15); };
-        *reinterpret_cast<uint32_t*>(img + offset(r)) = hi_word;
-        *reinterpret_cast<uint32_t*>(img + offset(RB + r)) = lo_word;
-        if (2 * RB + r < LY::N) *reinterpret_cast<uint32_t*>(img + offset(2 * RB + r)) = 0u;
+        auto offset = [&](int n) { return (n >> 3) * (8 * HD) + (d >> 4) * 128 + (n & 7) * 16 + (d & 15); };
+        if (has_d) {
+            *reinterpret_cast<uint32_t*>(img + offset(r)) = hi_word;
+            *reinterpret_cast<uint32_t*>(img + offset(RB + r)) = lo_word;
+            if (2 * RB + r < LY::N) *reinterpret_cast<uint32_t*>(img + offset(2 * RB + r)) = 0u;
+        }
         if (lane == 0) reinterpret_cast<float*>(img + LY::kQCodes)[r] = factor;
         return;
     }
@@ -1112,20 +1129,23 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D map over the pool's codes as rows of 128 bytes; one box = one page
-// (block_size rows), 128-byte swizzle to match the MMA operand layout.
+// 2-D map over the pool's codes as rows of head_dim bytes; one box = one
+// page (block_size rows), swizzled (128-byte rows: 128B, 64-byte rows: 64B)
+// to match the MMA operand layout.
 bool make_page_map(CUtensorMap* map, const int8_t* codes, const Pool& p) {
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return false;
+    const int64_t hd = p.head_dim;
     const int64_t last = (p.num_blocks - 1) * p.cbs + (p.num_layers - 1) * p.cls + (p.num_heads - 1) * p.chs;
-    const uint64_t rows = static_cast<uint64_t>(last / kHeadDim + p.block_size);
+    const uint64_t rows = static_cast<uint64_t>(last / hd + p.block_size);
     if (rows > (uint64_t(1) << 31)) return false;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(rows)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHeadDim)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kHeadDim), static_cast<cuuint32_t>(p.block_size)};
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(hd)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(hd), static_cast<cuuint32_t>(p.block_size)};
     cuuint32_t elem[2] = {1, 1};
+    const CUtensorMapSwizzle swizzle = hd == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(codes), dims, strides, box, elem,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -1178,13 +1198,13 @@ int num_sms() {
     return sms;
 }
 
-template <int RB>
+template <int RB, int HD>
 sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap,
                            const CUtensorMap& ksmap, const CUtensorMap& vsmap, int32_t* first, cudaStream_t st) {
-    using LY = Rows<RB>;
+    using LY = Rows<RB, HD>;
     const int64_t query_warps = t.a.batch * t.a.kv_heads * t.splits * RB;
-    prep_kernel<RB><<<static_cast<unsigned>(1 + (query_warps + 7) / 8), 256, 0, st>>>(t, first);
-    auto kernel = attn_tc_kernel<RB>;
+    prep_kernel<RB, HD><<<static_cast<unsigned>(1 + (query_warps + 7) / 8), 256, 0, st>>>(t, first);
+    auto kernel = attn_tc_kernel<RB, HD>;
     static bool configured = false;
     if (!configured) {
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::kDynamicSmem) !=
@@ -1212,14 +1232,14 @@ sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUten
 }  // namespace
 
 bool shape_supported(int64_t head_dim, int64_t rows) {
-    return head_dim == kHeadDim && rows >= 1 && splits_for(rows) <= kMaxSplits && bucket_for(split_rows(rows)) != 0;
+    return (head_dim == 64 || head_dim == 128) && rows >= 1 && splits_for(rows) <= kMaxSplits && bucket_for(split_rows(rows)) != 0;
 }
 
 bool supports(const AttnArgs& a) {
     const Pool& p = a.pool;
     const int64_t bs = p.block_size;
     return shape_supported(p.head_dim, a.rows) && bs >= 8 && bs <= kTile && (kTile % bs) == 0 &&
-           p.cbs % kHeadDim == 0 && p.cls % kHeadDim == 0 && p.chs % kHeadDim == 0 && p.sbs % 4 == 0 &&
+           p.cbs % p.head_dim == 0 && p.cls % p.head_dim == 0 && p.chs % p.head_dim == 0 && p.sbs % 4 == 0 &&
            p.sls % 4 == 0 && p.shs % 4 == 0 && (reinterpret_cast<uintptr_t>(p.key_scales) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(p.value_scales) & 15) == 0 && encode_fn() != nullptr;
 }
@@ -1239,7 +1259,7 @@ size_t extra_workspace(int64_t batch, int64_t kv_heads, int64_t max_chunks, int6
     auto up = [](int64_t v) { return static_cast<size_t>((v + 255) / 256 * 256); };
     const int64_t sp = splits_for(rows);
     return up(batch * kv_heads * max_chunks * sp * static_cast<int64_t>(sizeof(WorkItem))) + up(16) +
-           up(batch * 4) + up(batch * kv_heads * sp * query_image_stride(bucket_for(split_rows(rows))));
+           up(batch * 4) + up(batch * kv_heads * sp * query_image_stride(bucket_for(split_rows(rows)), 128));
 }
 
 sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
@@ -1269,14 +1289,21 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
         vsmap = vmap;
     }
     sdc_status_t rc;
+    const bool hd64 = a.pool.head_dim == 64;
+#define SDC_TC_BUCKET(R)                                                                            \
+    case R:                                                                                         \
+        rc = hd64 ? launch_bucket<R, 64>(t, kmap, vmap, ksmap, vsmap, first, st)                    \
+                  : launch_bucket<R, 128>(t, kmap, vmap, ksmap, vsmap, first, st);                  \
+        break;
     switch (bucket_for(t.rows)) {
-        case 8: rc = launch_bucket<8>(t, kmap, vmap, ksmap, vsmap, first, st); break;
-        case 16: rc = launch_bucket<16>(t, kmap, vmap, ksmap, vsmap, first, st); break;
-        case 20: rc = launch_bucket<20>(t, kmap, vmap, ksmap, vsmap, first, st); break;
-        case 24: rc = launch_bucket<24>(t, kmap, vmap, ksmap, vsmap, first, st); break;
-        case 32: rc = launch_bucket<32>(t, kmap, vmap, ksmap, vsmap, first, st); break;
+        SDC_TC_BUCKET(8)
+        SDC_TC_BUCKET(16)
+        SDC_TC_BUCKET(20)
+        SDC_TC_BUCKET(24)
+        SDC_TC_BUCKET(32)
         default: return SDC_STATUS_UNSUPPORTED;
     }
+#undef SDC_TC_BUCKET
     if (rc != SDC_STATUS_OK) return rc;
     return launch_attention_combine(a, st, /*programmatic=*/true);
 }
