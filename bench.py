@@ -391,24 +391,24 @@ def run_speculative(seed: int, device, world: int):
     draft = _random_llama(sp["draft"], sp["vocab"], device)
     target = _random_llama(sp["target"], sp["vocab"], device)
     B = sp["batch"]
+    # pool: every sequence at twice the new tokens on average; the block
+    # tables allow the decoder's worst case for one sequence
     tokens = sp["prompt"] + 2 * sp["new_tokens"] + 2 * sp["max_window"]
     blocks = B * (-(-tokens // 16) + 1)
 
     def cache(spec):
+        longest = sp["prompt"] + sp["new_tokens"] * (sp["max_window"] + 1) + 2 * sp["max_window"] + 2
         return PagedKVCache(KVCacheConfig(spec["layers"], spec["kv_heads"], spec["head_dim"], block_size=16,
-                                          num_blocks=blocks), device=device, max_sequences=B, check_status=False)
+                                          num_blocks=blocks), device=device, max_sequences=B, check_status=False,
+                            max_blocks_per_sequence=-(-longest // 16) + 1)
 
     dec = BatchedSpeculativeDecoder(draft, target, cache(sp["draft"]), cache(sp["target"]),
                                     window=DraftWindow(sp["window"], sp["min_window"], sp["max_window"]),
-                                    temperature=sp["temperature"], seed=seed)
+                                    temperature=sp["temperature"], seed=seed, cuda_graphs=True)
     rng = np.random.default_rng(seed)
     prompts = torch.from_numpy(rng.integers(0, sp["vocab"], size=(B, sp["prompt"]), dtype=np.int64)).to(device)
-    with torch.no_grad():
-        dec.generate(prompts, 8)  # warm-up: kernels, workspaces, allocator
+    def timed_run():
         dec.window.size = sp["window"]
-        for session in (dec.draft, dec.target):
-            session.timed = True
-            session.timings.clear()
         start, prefilled, end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         barrier(world)
         torch.cuda.synchronize()
@@ -416,8 +416,19 @@ def run_speculative(seed: int, device, world: int):
         result = dec.generate(prompts, sp["new_tokens"], prefill_done=prefilled)
         end.record()
         torch.cuda.synchronize()
-    prefill_ms = start.elapsed_time(prefilled)
-    decode_ms = prefilled.elapsed_time(end)
+        return result, start.elapsed_time(prefilled), prefilled.elapsed_time(end)
+
+    with torch.no_grad():
+        # decoding passes replayed from CUDA graphs: warm-up (eager first
+        # passes, capture of the second), then the timed run
+        dec.generate(prompts, 16)
+        result, prefill_ms, decode_ms = timed_run()
+        # the same run with eager passes and every attention call timed
+        dec.cuda_graphs = False
+        for session in (dec.draft, dec.target):
+            session.timed = True
+            session.timings.clear()
+        eager_result, eager_prefill_ms, eager_decode_ms = timed_run()
     attn = {}
     for name, session in (("draft", dec.draft), ("target", dec.target)):
         ms, nbytes = session.attention_time()
@@ -426,6 +437,7 @@ def run_speculative(seed: int, device, world: int):
     peak, peak_kind = measured_peaks()
     tokens_out = B * sp["new_tokens"]
     decode_max = max_over_ranks(decode_ms, world)
+    eager_max = max_over_ranks(eager_decode_ms, world)
     attn_ms = sum(v[0] for v in attn.values())
     attn_bytes = sum(v[1] for v in attn.values())
     stats = result.stats
@@ -439,10 +451,12 @@ def run_speculative(seed: int, device, world: int):
         "tokens_per_s_with_prefill": sum_over_ranks(tokens_out, world) / (max_over_ranks(prefill_ms + decode_ms, world) / 1e3),
         "decode_ms": decode_max,
         "prefill_ms": max_over_ranks(prefill_ms, world),
+        "decoding_passes": "CUDA graphs (draft steps and verify windows captured once, replayed)",
+        "tokens_per_s_eager_passes": sum_over_ranks(tokens_out, world) / (eager_max / 1e3),
         "acceptance_rate": stats.acceptance_rate,
         "verification_rounds": stats.verification_rounds,
-        "attention_ms": attn_ms,
-        "attention_share_of_run": attn_ms / (prefill_ms + decode_ms),
+        "attention_ms_eager_run": attn_ms,
+        "attention_share_of_eager_run": attn_ms / (eager_prefill_ms + eager_decode_ms),
         "attention_gbs": attn_bytes / (attn_ms / 1e3) / 1e9 if attn_ms > 0 else None,
         "attention_fraction_of_peak": attn_bytes / (attn_ms / 1e3) / 1e9 / peak if attn_ms > 0 else None,
         "attention_calls": {k: v[2] for k, v in attn.items()},

@@ -34,7 +34,7 @@ import math
 from typing import Hashable, Sequence
 
 from .cuda_kv_cache import PagedVerifyAttention
-from .kv_cache import PagedKVCache
+from .kv_cache import LayerwiseAppend, PagedKVCache
 
 _ACTIVE: list["PagedAttentionSession"] = []
 _MAX_ROWS = 64  # query rows per KV head one kernel call serves
@@ -79,6 +79,10 @@ class PagedAttentionSession:
         self.timed = False
         self.timings: list = []
         self._lengths: list[int] = []
+        # fixed_step state: attention with its own workspace, so that device
+        # addresses recorded in a CUDA graph stay valid
+        self._fixed_attention: PagedVerifyAttention | None = None
+        self._active_attention = self.attention
         register()
 
     @contextlib.contextmanager
@@ -100,6 +104,56 @@ class PagedAttentionSession:
             _ACTIVE.remove(self)
             self._pending = None
             self._inputs = None
+        self.cache.check_status()
+
+    def reserve_fixed_workspace(self, nbytes: int) -> None:
+        """Size the workspace used inside ``fixed_step`` once, before any CUDA
+        graph is captured: a captured graph keeps the address."""
+        import torch
+
+        if self._fixed_attention is None:
+            self._fixed_attention = PagedVerifyAttention.for_cache(self.cache)
+        fa = self._fixed_attention
+        if fa._workspace is None or fa._workspace.numel() < nbytes:
+            if fa._workspace is not None:
+                raise PagedAttentionError("the fixed workspace is already in use and cannot grow")
+            fa._workspace = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=self.cache.device)
+
+    @contextlib.contextmanager
+    def fixed_step(self, sequence_ids: Sequence[Hashable], new_tokens: int, slots, max_len: int):
+        """``step`` with device addresses that do not change from step to
+        step, for a forward pass captured once in a CUDA graph and replayed:
+        the reserved slots are copied into ``slots`` (int64 ``[B *
+        new_tokens]``), attention reads the cache's own block-table and
+        length rows (the sequences must occupy consecutive rows) with the
+        context bound ``max_len`` (at least every sequence's new length),
+        and its workspace is the one ``reserve_fixed_workspace`` sized."""
+        if self._pending is not None:
+            raise PagedAttentionError("a step is already open")
+        if self._fixed_attention is None or self._fixed_attention._workspace is None:
+            raise PagedAttentionError("reserve_fixed_workspace must size the workspace first")
+        self._ids = list(sequence_ids)
+        self._new = int(new_tokens)
+        pending = self.cache.reserve(self._ids, self._new)
+        slots[:pending.tokens].copy_(pending.slots)
+        self._pending = LayerwiseAppend(pending.plan, slots, pending.tokens)
+        tables, lens, longest = self.cache.attention_inputs(self._ids)
+        if tables.data_ptr() != self.cache.block_tables[self.cache.table_row(self._ids[0])].data_ptr():
+            self._pending = None
+            raise PagedAttentionError("fixed_step needs the sequences in consecutive cache rows")
+        if longest > max_len:
+            self._pending = None
+            raise PagedAttentionError(f"a sequence is {longest} tokens long, beyond the bound {max_len}")
+        self._inputs = (tables, lens, int(max_len))
+        self._active_attention = self._fixed_attention
+        _ACTIVE.append(self)
+        try:
+            yield self
+        finally:
+            _ACTIVE.remove(self)
+            self._pending = None
+            self._inputs = None
+            self._active_attention = self.attention
         self.cache.check_status()
 
     def forward(self, module, query, key, value, scaling, dropout):
@@ -135,8 +189,8 @@ class PagedAttentionSession:
         return out.transpose(1, 2).contiguous(), None
 
     def _attend(self, query, tables, lens, max_len, layer, behind):
-        if not self.timed:
-            return self.attention(query, tables, lens, max_len, layer)
+        if not self.timed or self._active_attention is not self.attention:
+            return self._active_attention(query, tables, lens, max_len, layer)
         import torch
 
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -139,7 +139,8 @@ class BatchedSpeculativeDecoder:
     """
 
     def __init__(self, draft_model, target_model, draft_cache: PagedKVCache, target_cache: PagedKVCache, *,
-                 window: DraftWindow | None = None, temperature: float = 1.0, seed: int = 0) -> None:
+                 window: DraftWindow | None = None, temperature: float = 1.0, seed: int = 0,
+                 cuda_graphs: bool = False) -> None:
         if draft_model.config.vocab_size != target_model.config.vocab_size:
             raise ValueError("draft and target models must share a vocabulary")
         if temperature < 0 or not math.isfinite(temperature):
@@ -152,6 +153,14 @@ class BatchedSpeculativeDecoder:
         self.temperature = float(temperature)
         self.seed = int(seed)
         self._tag = 0
+        # CUDA graphs of the decoding passes (draft single-token steps and
+        # target verify windows), one per (model, tokens per sequence),
+        # captured the second time a shape runs and replayed after that
+        self.cuda_graphs = bool(cuda_graphs)
+        self._graphs: dict = {}
+        self._seen: set = set()
+        self._bound = 0
+        self._batch = 0
         for model in (draft_model, target_model):
             model.set_attn_implementation(PagedAttentionSession.NAME)
 
@@ -168,6 +177,64 @@ class BatchedSpeculativeDecoder:
         with session.step(ids, n):
             out = model(input_ids=tokens, position_ids=positions, use_cache=False, logits_to_keep=keep)
         return out.logits
+
+    def _graphed_forward(self, session: PagedAttentionSession, model, ids: Sequence[Hashable], tokens, keep: int):
+        """``_forward`` through a CUDA graph: the host plans the step
+        (``fixed_step`` reserves the slots and copies them, the token ids and
+        positions into the graph's own buffers) and replays the recorded
+        passes; the first pass of a shape runs eagerly, the second is
+        captured."""
+        import torch
+
+        cache = session.cache
+        B, n = tokens.shape
+        key = (id(session), n, keep)
+        g = self._graphs.get(key)
+        if g is None:
+            g = {"tokens": torch.zeros((B, n), dtype=torch.long, device=tokens.device),
+                 "positions": torch.zeros((B, n), dtype=torch.long, device=tokens.device),
+                 "slots": torch.zeros(B * n, dtype=torch.int64, device=tokens.device),
+                 "graph": None, "logits": None}
+            self._graphs[key] = g
+        # a captured graph reads the table / length rows at fixed addresses
+        rows_at = cache.block_tables[cache.table_row(ids[0])].data_ptr()
+        if g.get("rows_at") != rows_at:
+            g["graph"], g["rows_at"] = None, rows_at
+            self._seen.discard(key)
+        lengths = torch.tensor([cache.sequence_length(s) for s in ids], device=tokens.device)
+        g["positions"].copy_(lengths[:, None] + torch.arange(n, device=tokens.device)[None, :])
+        g["tokens"].copy_(tokens)
+        with session.fixed_step(ids, n, g["slots"], self._bound):
+            if g["graph"] is not None:
+                g["graph"].replay()
+            elif key not in self._seen:
+                self._seen.add(key)
+                g["logits"] = model(input_ids=g["tokens"], position_ids=g["positions"], use_cache=False,
+                                    logits_to_keep=keep).logits
+            else:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    g["logits"] = model(input_ids=g["tokens"], position_ids=g["positions"], use_cache=False,
+                                        logits_to_keep=keep).logits
+                g["graph"] = graph
+                graph.replay()
+        return g["logits"]
+
+    def _prepare_graphs(self, B: int, bound: int) -> None:
+        """Fixed workspaces for the graphed passes (sized for every window the
+        decoder can use) and a fresh set of graphs when the batch or the
+        context bound changes."""
+        if B == self._batch and bound <= self._bound:
+            return
+        self._graphs.clear()
+        self._seen.clear()
+        self._batch, self._bound = B, bound
+        for session, model in ((self.draft, self.draft_model), (self.target, self.target_model)):
+            c = model.config
+            need = max(session.attention.workspace_bytes(B, c.num_attention_heads, w, bound)
+                       for w in range(1, self.window.max_size + 2))
+            session._fixed_attention = None
+            session.reserve_fixed_workspace(need)
 
     def _prefill(self, session: PagedAttentionSession, model, ids, tokens, chunk: int) -> None:
         for i in range(0, tokens.shape[1], chunk):
@@ -200,6 +267,12 @@ class BatchedSpeculativeDecoder:
                 self._prefill(self.draft, self.draft_model, ids, ctx, prefill_chunk)
                 self._prefill(self.target, self.target_model, ids, ctx, prefill_chunk)
             last = prompts[:, -1:]
+            if self.cuda_graphs:
+                # a round adds 1 to max_size + 1 tokens to every sequence and
+                # rounds continue until the slowest has max_new_tokens, so no
+                # context grows beyond this bound during the call
+                step = self.window.max_size + 1
+                self._prepare_graphs(B, int(prompts.shape[1]) + int(max_new_tokens) * step + step + 1)
             if prefill_done is not None:
                 prefill_done.record()
             while min(len(g) for g in generated) < max_new_tokens:
@@ -222,8 +295,9 @@ class BatchedSpeculativeDecoder:
         # fully accepted window leaves the draft cache complete
         feed = last
         proposals, draft_probs = [], []
+        forward = self._graphed_forward if self.cuda_graphs else self._forward
         for i in range(k + 1):
-            logits = self._forward(self.draft, self.draft_model, ids, feed, 1)[:, -1]
+            logits = forward(self.draft, self.draft_model, ids, feed, 1)[:, -1]
             if i == k:
                 break
             if greedy:
@@ -237,7 +311,7 @@ class BatchedSpeculativeDecoder:
         drafts = torch.cat(proposals, dim=1)  # [B, k]
         # target: one verify pass over last, d_1 .. d_k
         verify = torch.cat([last, drafts], dim=1)
-        tlogits = self._forward(self.target, self.target_model, ids, verify, k + 1)  # [B, k + 1, V]
+        tlogits = forward(self.target, self.target_model, ids, verify, k + 1)  # [B, k + 1, V]
         if greedy:
             accepted, new_tok = accept_greedy(drafts, tlogits)
         else:

@@ -9,7 +9,8 @@ run for a batch with both models attending through the device kernels.
   over the same INT8 cache (total-variation distance within sampling noise),
   although the draft's distribution is far from it;
 * the caches hold exactly the committed tokens but the last after every
-  round, and ``generate`` leaves no sequence behind.
+  round, and ``generate`` leaves no sequence behind;
+* decoding passes replayed from CUDA graphs behave as the eager ones.
 """
 
 from __future__ import annotations
@@ -46,16 +47,16 @@ def _decoder(device, draft, target, sequences, tokens, **kwargs):
                                      _cache_for(device, target, sequences, tokens), **kwargs)
 
 
-@pytest.mark.parametrize("temperature", [1.0, 0.0])
-def test_identical_models_accept_the_window(device, temperature):
+@pytest.mark.parametrize("temperature,graphs", [(1.0, False), (0.0, False), (1.0, True)])
+def test_identical_models_accept_the_window(device, temperature, graphs):
     import torch
 
     from specdecode_b200.speculative import DraftWindow
 
     model = _llama(device, layers=2, hidden=512, heads=4, kv_heads=1, head_dim=128, vocab=1000, init=0.05, seed=1)
     B, P, new = 8, 21, 24
-    dec = _decoder(device, model, model, B, P + new + 16, window=DraftWindow(5, dynamic=False),
-                   temperature=temperature, seed=3)
+    dec = _decoder(device, model, model, B, P + new * 7 + 16, window=DraftWindow(5, dynamic=False),
+                   temperature=temperature, seed=3, cuda_graphs=graphs)
     prompts = torch.randint(0, 1000, (B, P), generator=torch.Generator().manual_seed(5))
     with torch.no_grad():
         result = dec.generate(prompts, new)
@@ -98,7 +99,8 @@ def test_first_token_follows_the_target_distribution(device):
     assert tv < 0.05, (tv, got, want)
 
 
-def test_caches_hold_the_committed_tokens(device):
+@pytest.mark.parametrize("graphs", [False, True])
+def test_caches_hold_the_committed_tokens(device, graphs):
     import torch
 
     from specdecode_b200.speculative import BatchedSpeculativeDecoder, DraftWindow
@@ -106,7 +108,8 @@ def test_caches_hold_the_committed_tokens(device):
     draft = _llama(device, layers=1, hidden=256, heads=4, kv_heads=2, head_dim=64, vocab=300, init=0.3, seed=4)
     target = _llama(device, layers=2, hidden=512, heads=4, kv_heads=1, head_dim=128, vocab=300, init=0.3, seed=5)
     B, P = 6, 9
-    dec = _decoder(device, draft, target, B, P + 64, window=DraftWindow(6, min_size=4, max_size=8), seed=1)
+    dec = _decoder(device, draft, target, B, P + 40 * 9 + 16, window=DraftWindow(6, min_size=4, max_size=8), seed=1,
+                   cuda_graphs=graphs)
     prompts = torch.randint(0, 300, (B, P), generator=torch.Generator().manual_seed(8))
     seen = []
     original = BatchedSpeculativeDecoder._round
@@ -131,3 +134,26 @@ def test_caches_hold_the_committed_tokens(device):
     s = result.stats
     assert s.accepted_tokens + s.rejected_tokens <= s.drafted_tokens
     assert s.target_tokens == B * s.verification_rounds
+
+
+def test_graphed_passes_match_eager_passes(device):
+    """Replaying the captured decoding passes gives the token streams that
+    running them eagerly gives (greedy verification, so the streams are a
+    deterministic function of the logits)."""
+    import torch
+
+    from specdecode_b200.speculative import DraftWindow
+
+    draft = _llama(device, layers=1, hidden=256, heads=4, kv_heads=2, head_dim=64, vocab=300, init=0.3, seed=4)
+    target = _llama(device, layers=2, hidden=512, heads=4, kv_heads=1, head_dim=128, vocab=300, init=0.3, seed=5)
+    B, P, new = 4, 13, 20
+    prompts = torch.randint(0, 300, (B, P), generator=torch.Generator().manual_seed(21))
+    streams = []
+    for graphs in (False, True):
+        dec = _decoder(device, draft, target, B, P + new * 9 + 16, window=DraftWindow(5, dynamic=False),
+                       temperature=0.0, seed=1, cuda_graphs=graphs)
+        with torch.no_grad():
+            dec.generate(prompts, 6)  # with graphs: eager first passes, then capture
+            streams.append(dec.generate(prompts, new).generated_tokens)
+    same = sum(a == b for a, b in zip(*streams))
+    assert same >= B - 1, streams
