@@ -83,6 +83,10 @@ class PagedAttentionSession:
         # addresses recorded in a CUDA graph stay valid
         self._fixed_attention: PagedVerifyAttention | None = None
         self._active_attention = self.attention
+        # read the cache's device fault word after every step (a device
+        # synchronisation); a caller that checks it itself less often, once
+        # it synchronises anyway, turns this off
+        self.check_each_step = True
         register()
 
     @contextlib.contextmanager
@@ -104,7 +108,8 @@ class PagedAttentionSession:
             _ACTIVE.remove(self)
             self._pending = None
             self._inputs = None
-        self.cache.check_status()
+        if self.check_each_step:
+            self.cache.check_status()
 
     def reserve_fixed_workspace(self, nbytes: int) -> None:
         """Size the workspace used inside ``fixed_step`` once, before any CUDA
@@ -154,7 +159,8 @@ class PagedAttentionSession:
             self._pending = None
             self._inputs = None
             self._active_attention = self.attention
-        self.cache.check_status()
+        if self.check_each_step:
+            self.cache.check_status()
 
     def forward(self, module, query, key, value, scaling, dropout):
         import torch

@@ -229,6 +229,15 @@ class _MetadataRing:
         base = self.dev[slot].data_ptr()
         return [base + off for off in offsets], slot
 
+    def device_view(self, ticket: int, address: int, count: int, dtype):
+        """``count`` elements of ``dtype`` at ``address`` inside ticket's
+        device buffer (valid until the ticket is released)."""
+        torch = _torch()
+        buf = self.dev[ticket]
+        start = address - buf.data_ptr()
+        nbytes = count * torch.empty((), dtype=dtype).element_size()
+        return buf[start:start + nbytes].view(dtype)
+
     def release(self, ticket: int, stream) -> None:
         torch = _torch()
         event = torch.cuda.Event()
@@ -312,7 +321,9 @@ class PagedKVCache:
         self.block_tables = torch.full(self._pages.tables.shape, -1, dtype=torch.int32, device=self.device)
         self.context_lens = torch.zeros(self._pages.tables.shape[0], dtype=torch.int32, device=self.device)
         self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self._meta = _MetadataRing(self.device)
+        # deep enough that a decoding loop planning several steps ahead of the
+        # device rarely waits for a ring slot
+        self._meta = _MetadataRing(self.device, depth=16)
         self.pool_desc = _lib.PagePool(
             self.key_codes.data_ptr(), self.value_codes.data_ptr(), self.key_scale_pages.data_ptr(),
             self.value_scale_pages.data_ptr(), nb, bs, L, H, D,
@@ -484,9 +495,12 @@ class PagedKVCache:
         plan = self._pages.plan_append(ids, [count] * len(ids))
         stream = self._stream()
         try:
-            slots = torch.from_numpy(np.ascontiguousarray(plan.slots, dtype=np.int64)).to(self.device)
-            (_, entries_ptr, lengths_ptr), ticket = self._meta.upload(
-                [plan.slots, plan.table_entries, plan.new_lengths], stream)
+            (slots_ptr, entries_ptr, lengths_ptr), ticket = self._meta.upload(
+                [np.ascontiguousarray(plan.slots, dtype=np.int64), plan.table_entries, plan.new_lengths], stream)
+            # the reservation keeps its own copy of the slots (a device-to-device
+            # copy on the stream: no host synchronisation)
+            with torch.cuda.stream(stream):
+                slots = self._meta.device_view(ticket, slots_ptr, int(plan.slots.size), torch.int64).clone()
         except Exception:
             self._pages.undo_append(plan)
             raise

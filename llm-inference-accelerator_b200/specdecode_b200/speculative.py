@@ -149,6 +149,10 @@ class BatchedSpeculativeDecoder:
         self.target_model = target_model
         self.draft = PagedAttentionSession(draft_cache)
         self.target = PagedAttentionSession(target_cache)
+        # the device fault words are read once per round, after the round's
+        # device-to-host read has synchronised anyway
+        self.draft.check_each_step = False
+        self.target.check_each_step = False
         self.window = window or DraftWindow()
         self.temperature = float(temperature)
         self.seed = int(seed)
@@ -201,10 +205,12 @@ class BatchedSpeculativeDecoder:
         if g.get("rows_at") != rows_at:
             g["graph"], g["rows_at"] = None, rows_at
             self._seen.discard(key)
-        lengths = torch.tensor([cache.sequence_length(s) for s in ids], device=tokens.device)
-        g["positions"].copy_(lengths[:, None] + torch.arange(n, device=tokens.device)[None, :])
         g["tokens"].copy_(tokens)
         with session.fixed_step(ids, n, g["slots"], self._bound):
+            # positions from the device lengths, which now include the n new
+            # tokens (no host-to-device copy, so no synchronisation)
+            lens = session._inputs[1]
+            g["positions"].copy_(lens[:, None].long() - n + torch.arange(n, device=tokens.device)[None, :])
             if g["graph"] is not None:
                 g["graph"].replay()
             elif key not in self._seen:
@@ -266,6 +272,8 @@ class BatchedSpeculativeDecoder:
                 ctx = prompts[:, :-1]
                 self._prefill(self.draft, self.draft_model, ids, ctx, prefill_chunk)
                 self._prefill(self.target, self.target_model, ids, ctx, prefill_chunk)
+                self.draft.cache.check_status()
+                self.target.cache.check_status()
             last = prompts[:, -1:]
             if self.cuda_graphs:
                 # a round adds 1 to max_size + 1 tokens to every sequence and
@@ -318,6 +326,8 @@ class BatchedSpeculativeDecoder:
             accepted, new_tok = accept_sampled(drafts, torch.stack(draft_probs, dim=1),
                                                _distribution(tlogits, self.temperature), gen)
         host = torch.cat([accepted[:, None], drafts, new_tok], dim=1).cpu().tolist()
+        self.draft.cache.check_status()
+        self.target.cache.check_status()
         keep_d, keep_t = [], []
         for b, row in enumerate(host):
             j = int(row[0])
