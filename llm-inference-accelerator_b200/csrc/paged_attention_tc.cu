@@ -126,6 +126,7 @@ struct TcArgs {
     int32_t splits;      // row splits per KV head
     int32_t total_rows;  // query rows per KV head (group x window)
     int32_t gather4;     // scales fetched four pages per copy through the scale maps
+    int32_t direct;      // one chunk per sequence: items write the output rows, no partials
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -305,6 +306,17 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // Low bytes of four words packed into one word (byte i from w_i).
 __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
     return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
+}
+
+// One output element in the query's dtype.
+__device__ __forceinline__ void store_output(const AttnArgs& a, int64_t index, float v) {
+    if (a.query_dtype == SDC_DTYPE_BF16) {
+        static_cast<__nv_bfloat16*>(a.out)[index] = __float2bfloat16_rn(v);
+    } else if (a.query_dtype == SDC_DTYPE_F16) {
+        static_cast<__half*>(a.out)[index] = __float2half_rn(v);
+    } else {
+        static_cast<float*>(a.out)[index] = v;
+    }
 }
 
 // ---------------------------------------------------------------- main kernel
@@ -920,20 +932,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     l_tot = l_lane * e0_lane + l1 * e1_lane;
                 }
-                const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
-                const int64_t chunk = it.chunk;
-                float* part_o = a.part_o + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * HD;
-                float* part_ml = a.part_ml + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * 2;
+                if (t.direct) {
+                    // every item covers its sequence's whole context: it writes
+                    // the normalised output rows itself (no partial, no combine)
+                    const float inv_lane = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+                    const int64_t q0 = (static_cast<int64_t>(it.b) * a.query_heads + it.h * a.group) * a.window + row0;
 #pragma unroll
-                for (int r = 0; r < RB; ++r) {
-                    const float e0 = __shfl_sync(kFullMask, e0_lane, r);
-                    const float e1 = __shfl_sync(kFullMask, e1_lane, r);
-                    const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
-                    if (r < R && o_row) part_o[r * HD + dcol] = o0 * e0 + merge_o[tid * RB + r] * e1;
-                }
-                if (qw == 0 && lane < R) {
-                    part_ml[2 * lane + 0] = m_tot;
-                    part_ml[2 * lane + 1] = l_tot;
+                    for (int r = 0; r < RB; ++r) {
+                        const float e0 = __shfl_sync(kFullMask, e0_lane, r);
+                        const float e1 = __shfl_sync(kFullMask, e1_lane, r);
+                        const float inv = __shfl_sync(kFullMask, inv_lane, r);
+                        const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
+                        if (r < R && o_row) {
+                            store_output(a, (q0 + r) * HD + dcol, (o0 * e0 + merge_o[tid * RB + r] * e1) * inv);
+                        }
+                    }
+                } else {
+                    const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
+                    const int64_t chunk = it.chunk;
+                    float* part_o = a.part_o + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * HD;
+                    float* part_ml = a.part_ml + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * 2;
+#pragma unroll
+                    for (int r = 0; r < RB; ++r) {
+                        const float e0 = __shfl_sync(kFullMask, e0_lane, r);
+                        const float e1 = __shfl_sync(kFullMask, e1_lane, r);
+                        const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
+                        if (r < R && o_row) part_o[r * HD + dcol] = o0 * e0 + merge_o[tid * RB + r] * e1;
+                    }
+                    if (qw == 0 && lane < R) {
+                        part_ml[2 * lane + 0] = m_tot;
+                        part_ml[2 * lane + 1] = l_tot;
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(mergeEmpty));
@@ -979,6 +1008,16 @@ __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
         unsigned char* img = t.qimg + image * LY::kQStride;
         const int d = lane * 4;
         const bool has_d = d < HD;
+        {
+            // a sequence whose context length is invalid gets no items: its
+            // output rows are zero
+            const int64_t T = __ldg(a.context_lens + b);
+            const bool valid = T >= a.window && T <= a.table_stride * a.pool.block_size && T <= a.max_chunks * a.chunk;
+            if (!valid && has_d && r < t.rows && row < t.total_rows) {
+                const int64_t e0 = ((b * a.query_heads + h * a.group) * a.window + row) * HD + d;
+                for (int i = 0; i < 4; ++i) store_output(a, e0 + i, 0.0f);
+            }
+        }
         float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (has_d && r < t.rows && row < t.total_rows) {
             const int64_t e = ((b * a.query_heads + h * a.group) * a.window + row) * HD + d;
@@ -1252,6 +1291,12 @@ int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len, int6
     c = (c + kTile - 1) / kTile * kTile;
     if (c < 512) c = 512;
     if (c > kMaxItemTiles * kTile) c = kMaxItemTiles * kTile;
+    // with at least two (sequence, KV head) items per SM, whole contexts
+    // balance well enough and need no combine
+    if (batch * kv_heads * splits_for(rows) >= 2 * static_cast<int64_t>(num_sms()) &&
+        max_context_len <= kMaxItemTiles * kTile) {
+        c = (max_context_len + kTile - 1) / kTile * kTile;
+    }
     return c;
 }
 
@@ -1270,6 +1315,7 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
     t.splits = static_cast<int32_t>(splits_for(a.rows));
     t.rows = static_cast<int32_t>(split_rows(a.rows));
     t.total_rows = static_cast<int32_t>(a.rows);
+    t.direct = a.max_chunks == 1 ? 1 : 0;
     t.items = reinterpret_cast<const WorkItem*>(base);
     base += up(a.batch * a.kv_heads * a.max_chunks * t.splits * static_cast<int64_t>(sizeof(WorkItem)));
     t.item_count = reinterpret_cast<const int32_t*>(base);
@@ -1305,6 +1351,7 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
     }
 #undef SDC_TC_BUCKET
     if (rc != SDC_STATUS_OK) return rc;
+    if (t.direct) return SDC_STATUS_OK;  // every item wrote its output rows
     return launch_attention_combine(a, st, /*programmatic=*/true);
 }
 
