@@ -992,6 +992,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // 64 lanes 16-31 of a row's warp hold no elements.
 template <int RB, int HD>
 __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
+    static_assert(kMaxItemTiles < 256, "one scan thread per size bin");
     using LY = Rows<RB, HD>;
     const AttnArgs& a = t.a;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the item kernel may start its set-up
@@ -1115,14 +1116,15 @@ __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
         add_to_bin(chunk_tiles(i, b, c, T), per_chunk);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {  // bin start positions, largest size first
-        int32_t running = 0;
-        for (int i = kMaxItemTiles; i >= 1; --i) {
-            const int32_t n = hist[i];
-            hist[i] = running;
-            running += n;
-        }
-        *const_cast<int32_t*>(t.item_count) = running;
+    {  // bin start positions, largest size first: thread i owns bin kMaxItemTiles - i
+        using Scan = cub::BlockScan<int32_t, 256>;
+        __shared__ typename Scan::TempStorage scan_tmp;
+        const int bin = kMaxItemTiles - static_cast<int>(threadIdx.x);
+        const int32_t n = bin >= 1 ? hist[bin] : 0;
+        int32_t start = 0, total = 0;
+        Scan(scan_tmp).ExclusiveSum(n, start, total);
+        if (bin >= 1) hist[bin] = start;
+        if (threadIdx.x == 0) *const_cast<int32_t*>(t.item_count) = total;
     }
     __syncthreads();
     for (int64_t i = threadIdx.x; i < span; i += blockDim.x) {
