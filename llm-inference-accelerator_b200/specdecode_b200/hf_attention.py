@@ -111,6 +111,19 @@ class PagedAttentionSession:
         if self.check_each_step:
             self.cache.check_status()
 
+    @property
+    def step_context_lens(self):
+        """Device int32 context lengths of the open step's sequences,
+        including the step's new tokens."""
+        if self._inputs is None:
+            raise PagedAttentionError("no step is open")
+        return self._inputs[1]
+
+    def release_fixed_workspace(self) -> None:
+        """Drop the ``fixed_step`` workspace (graphs that recorded its address
+        must be dropped with it)."""
+        self._fixed_attention = None
+
     def reserve_fixed_workspace(self, nbytes: int) -> None:
         """Size the workspace used inside ``fixed_step`` once, before any CUDA
         graph is captured: a captured graph keeps the address."""

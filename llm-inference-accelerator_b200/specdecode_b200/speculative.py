@@ -209,7 +209,7 @@ class BatchedSpeculativeDecoder:
         with session.fixed_step(ids, n, g["slots"], self._bound):
             # positions from the device lengths, which now include the n new
             # tokens (no host-to-device copy, so no synchronisation)
-            lens = session._inputs[1]
+            lens = session.step_context_lens
             g["positions"].copy_(lens[:, None].long() - n + torch.arange(n, device=tokens.device)[None, :])
             if g["graph"] is not None:
                 g["graph"].replay()
@@ -239,7 +239,7 @@ class BatchedSpeculativeDecoder:
             c = model.config
             need = max(session.attention.workspace_bytes(B, c.num_attention_heads, w, bound)
                        for w in range(1, self.window.max_size + 2))
-            session._fixed_attention = None
+            session.release_fixed_workspace()
             session.reserve_fixed_workspace(need)
 
     def _prefill(self, session: PagedAttentionSession, model, ids, tokens, chunk: int) -> None:
