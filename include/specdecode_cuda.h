@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define SDC_ABI_VERSION UINT32_C(0x00020001)
+#define SDC_ABI_VERSION UINT32_C(0x00020002)
 
 /* Values 0-10 keep the meaning they have in the reference's sd_status_t
  * (native/include/specdecode/native.h:25-37). */
@@ -49,6 +49,10 @@ typedef enum sdc_status {
     SDC_STATUS_NULL_ARGUMENT = 1,
     SDC_STATUS_INVALID_SIZE = 2,
     SDC_STATUS_NONFINITE_VALUE = 3,
+    SDC_STATUS_NEGATIVE_PROBABILITY = 4,
+    SDC_STATUS_ZERO_MASS = 5,
+    SDC_STATUS_TOKEN_OUT_OF_RANGE = 6,
+    SDC_STATUS_INVALID_UNIFORM = 7,
     SDC_STATUS_OVERFLOW = 8,
     SDC_STATUS_INTERNAL_ERROR = 9,
     SDC_STATUS_INVALID_SCALE = 10,
@@ -68,6 +72,12 @@ typedef enum sdc_status {
 #define SDC_FAULT_CONTEXT_RANGE    0x10
 #define SDC_FAULT_WAIT_TIMEOUT     0x20
 #define SDC_FAULT_TABLE_RANGE      0x40
+/* Sampling kernels (the reference's status for the same input in brackets). */
+#define SDC_FAULT_NEGATIVE_WEIGHT  0x80   /* a weight < 0, or a probability outside [0, 1] [4] */
+#define SDC_FAULT_ZERO_MASS        0x100  /* a row whose weights sum to 0 [5] */
+#define SDC_FAULT_TOKEN_RANGE      0x200  /* a proposed token outside the vocabulary [6] */
+#define SDC_FAULT_INVALID_UNIFORM  0x400  /* a uniform outside [0, 1) [7] */
+#define SDC_FAULT_PROPOSAL_COUNT   0x800  /* a proposal count outside [1, proposals] */
 
 typedef enum sdc_dtype {
     SDC_DTYPE_F32 = 0,
@@ -200,17 +210,6 @@ SDC_API sdc_status_t sdc_paged_verify_attention(
     int64_t table_stride, const int32_t* context_lens, int64_t max_context_len, void* out,
     void* workspace, size_t workspace_bytes, int32_t* device_status, uintptr_t stream);
 
-/*
- * Gather and dequantize cached tokens: for every slot i and layer in
- * [layer_begin, layer_begin + num_layers) and head, writes code * scale to
- * out_keys / out_values at i*out_token_stride + (layer-layer_begin)*out_layer_stride
- * + head*out_head_stride (dim contiguous) in out_dtype.  f64 output is exact;
- * f32 is the correctly rounded product; bf16/f16 narrow through float32, as
- * torch.tensor does for Python floats.
- * Replaces: PagedKVCache.read_token / read_sequence dequantization
- * (src/specdecode/kv_cache.py:349-380) and the CPU reconstruct of
- * HuggingFacePagedCacheMirror.materialize_legacy_cache (src/specdecode/hf_paged_cache.py:247-313).
- */
 /* Bytes of the library-owned scratch of sdc_paged_verify_attention_no_alloc. */
 #define SDC_NO_ALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 
@@ -235,11 +234,134 @@ SDC_API sdc_status_t sdc_paged_verify_attention_no_alloc(
     int64_t table_stride, const int32_t* context_lens, int64_t max_context_len, void* out,
     int32_t* device_status, uintptr_t stream);
 
+/*
+ * Gather and dequantize cached tokens: for every slot i and layer in
+ * [layer_begin, layer_begin + num_layers) and head, writes code * scale to
+ * out_keys / out_values at i*out_token_stride + (layer-layer_begin)*out_layer_stride
+ * + head*out_head_stride (dim contiguous) in out_dtype.  f64 output is exact;
+ * f32 is the correctly rounded product; bf16/f16 narrow through float32, as
+ * torch.tensor does for Python floats.
+ * Replaces: PagedKVCache.read_token / read_sequence dequantization
+ * (src/specdecode/kv_cache.py:349-380) and the CPU reconstruct of
+ * HuggingFacePagedCacheMirror.materialize_legacy_cache (src/specdecode/hf_paged_cache.py:247-313).
+ */
 SDC_API sdc_status_t sdc_gather_dequantize(
     const sdc_page_pool_t* pool, int64_t layer_begin, int64_t num_layers,
     const int64_t* slot_mapping, int64_t num_tokens, void* out_keys, void* out_values,
     int out_dtype, int64_t out_token_stride, int64_t out_layer_stride, int64_t out_head_stride,
     int32_t* device_status, uintptr_t stream);
+
+/*
+ * Device-resident acceptance and sampling (batched device forms of the
+ * reference's sampling functions, native/include/specdecode/native.h:43-87,
+ * native/src/native.cpp:84-273).
+ *
+ * Probability rows are device arrays of non-negative weights in dtype
+ * SDC_DTYPE_F32 or SDC_DTYPE_F64, `vocab` (1 .. 2^21) weights per row, rows
+ * `row_stride` elements apart; they need not be normalised.  Each function
+ * validates its weights as the reference does (finite, non-negative, positive
+ * sum), but on the device: a row that fails ORs the SDC_FAULT_* bit into
+ * `device_status` and gets the marker output stated below instead of a
+ * result.  Host-visible arguments (pointers, sizes, strides) are checked
+ * before any launch.
+ *
+ * Arithmetic: sums are double-double (error below 2^-100 of the sum), the
+ * per-row quotients double-double, so every decision (threshold < running
+ * sum, uniform < probability) equals the reference's except for a draw
+ * within about 1e-16 relative of the boundary, and every probability output
+ * is within 2 ulp of the reference's extended-precision result.
+ */
+
+/* out[r][v] = weights[r][v] / sum(weights[r]), f64.  Replaces sd_normalize_f64
+ * (native.h:43, native.cpp:84-102).  Faulted rows are not written. */
+SDC_API sdc_status_t sdc_normalize_rows(
+    const void* weights, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+    double* output, int64_t output_stride, int32_t* device_status, uintptr_t stream);
+
+/* output_tokens[r] = the first v with uniforms[r] * sum(weights[r]) < weights[r][0] + ... +
+ * weights[r][v], or vocab - 1 if there is none; -1 for a faulted row.
+ * Replaces sd_sample_categorical_f64 (native.h:46-51, native.cpp:104-136). */
+SDC_API sdc_status_t sdc_sample_categorical_rows(
+    const void* weights, int dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+    const double* uniforms, int64_t* output_tokens, int32_t* device_status, uintptr_t stream);
+
+/* out[r][v] = max(0, target[r][v] / sum(target[r]) - draft[r][v] / sum(draft[r])), or
+ * target[r][v] / sum(target[r]) when those sum to at most 1e-15.  Faulted rows are
+ * not written.  Replaces sd_residual_weights_f64 (native.h:57-62, native.cpp:138-177). */
+SDC_API sdc_status_t sdc_residual_weights_rows(
+    const void* target, const void* draft, int dtype, int64_t rows, int64_t vocab,
+    int64_t target_stride, int64_t draft_stride, double* output, int64_t output_stride,
+    int32_t* device_status, uintptr_t stream);
+
+/* out[r] = 1 if draft[r][t] == 0, else min(1, (target[r][t] / sum(target[r])) /
+ * (draft[r][t] / sum(draft[r]))) with t = proposed_tokens[r]; NaN for a faulted row.
+ * Replaces sd_acceptance_probabilities_f64 (native.h:68-75, native.cpp:179-232). */
+SDC_API sdc_status_t sdc_acceptance_probabilities_rows(
+    const void* target, const void* draft, int dtype, int64_t rows, int64_t vocab,
+    int64_t target_stride, int64_t draft_stride, const int64_t* proposed_tokens,
+    double* output_probabilities, int32_t* device_status, uintptr_t stream);
+
+/* For each of `sequences` rows of `proposals` acceptance probabilities and
+ * uniforms (both `row_stride` apart): output_accepted[s] = the first i with
+ * !(uniforms[s][i] < probabilities[s][i]), or `proposals` if none; -1 for a
+ * faulted row.  Replaces sd_first_rejection_f64 (native.h:81-87,
+ * native.cpp:234-273), whose two outputs are both this index. */
+SDC_API sdc_status_t sdc_first_rejection_rows(
+    const double* acceptance_probabilities, const double* uniforms, int64_t sequences,
+    int64_t proposals, int64_t row_stride, int64_t* output_accepted, int32_t* device_status,
+    uintptr_t stream);
+
+/*
+ * One verification round of speculative sampling for a batch: sequence s
+ * proposed tokens proposed_tokens[s][0 .. n_s), drawn from the draft rows
+ * (s, 0 .. n_s); the target rows (s, 0 .. n_s] are the target's distributions
+ * at the same positions plus the bonus position.  Row (s, i) of the target
+ * starts at target_rows + s * target_sequence_stride + i * target_row_stride
+ * elements, likewise for the draft.
+ *
+ * uniforms[s][0 .. n_s] hold the sequence's draws in the reference decoder's
+ * order (src/specdecode/decoder.py:206-257, docs/native.md:58-73): draw i
+ * decides proposal i (accepted iff draw < its acceptance probability); after
+ * a rejection at j, draw j + 1 samples the correction from the residual
+ * weights of row j; after a full acceptance, draw n_s samples the bonus
+ * token from target row n_s.  A caller holding one uniform stream per
+ * sequence therefore consumes exactly output_accepted[s] + 2 draws after a
+ * rejection and n_s + 1 (or n_s, without a bonus) after a full acceptance.
+ *
+ * n_s = proposal_counts[s] (1 .. proposals), or `proposals` when
+ * proposal_counts is NULL.  bonus_allowed[s] == 0 means a full acceptance
+ * ends the round without a bonus draw (the reference stops at an accepted
+ * end-of-sequence token or at the token budget); NULL allows every bonus.
+ *
+ * Outputs: output_probabilities[s][i] (stride `proposals`) for i < n_s;
+ * output_accepted[s] = accepted proposals; output_tokens[s] = the correction
+ * or bonus token, or -1 after a full acceptance without a bonus.  A faulted
+ * sequence gets -1 in both.  Two launches: one block per (sequence,
+ * proposal) for the acceptance probabilities, then one per sequence for the
+ * decision and the sample.
+ */
+typedef struct sdc_verify_batch {
+    const void* target_rows;
+    const void* draft_rows;
+    int dtype;
+    int64_t sequences;
+    int64_t proposals;
+    int64_t vocab;
+    int64_t target_sequence_stride;
+    int64_t target_row_stride;
+    int64_t draft_sequence_stride;
+    int64_t draft_row_stride;
+    const int64_t* proposed_tokens;  /* [sequences][token_stride] */
+    int64_t token_stride;
+    const double* uniforms;          /* [sequences][uniform_stride], uniform_stride > proposals */
+    int64_t uniform_stride;
+    const int64_t* proposal_counts;  /* [sequences] or NULL */
+    const uint8_t* bonus_allowed;    /* [sequences] or NULL */
+} sdc_verify_batch_t;
+
+SDC_API sdc_status_t sdc_speculative_verify(
+    const sdc_verify_batch_t* batch, double* output_probabilities, int64_t* output_accepted,
+    int64_t* output_tokens, int32_t* device_status, uintptr_t stream);
 
 #ifdef __cplusplus
 }

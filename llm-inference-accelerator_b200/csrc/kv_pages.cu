@@ -533,6 +533,10 @@ SDC_API const char* sdc_status_string(sdc_status_t status) {
         case SDC_STATUS_NULL_ARGUMENT: return "null argument";
         case SDC_STATUS_INVALID_SIZE: return "invalid size";
         case SDC_STATUS_NONFINITE_VALUE: return "non-finite value";
+        case SDC_STATUS_NEGATIVE_PROBABILITY: return "negative probability";
+        case SDC_STATUS_ZERO_MASS: return "zero probability mass";
+        case SDC_STATUS_TOKEN_OUT_OF_RANGE: return "token out of range";
+        case SDC_STATUS_INVALID_UNIFORM: return "uniform must be finite and in [0, 1)";
         case SDC_STATUS_OVERFLOW: return "size overflow";
         case SDC_STATUS_INTERNAL_ERROR: return "internal error";
         case SDC_STATUS_INVALID_SCALE: return "invalid quantization scale";

@@ -15,7 +15,7 @@ import os
 import threading
 from pathlib import Path
 
-ABI_VERSION = 0x00020001
+ABI_VERSION = 0x00020002
 LIBRARY_NAME = "libspecdecode_cuda.so"
 _ENV = "SPECDECODE_CUDA_LIBRARY"
 
@@ -23,6 +23,10 @@ STATUS_OK = 0
 STATUS_NULL_ARGUMENT = 1
 STATUS_INVALID_SIZE = 2
 STATUS_NONFINITE_VALUE = 3
+STATUS_NEGATIVE_PROBABILITY = 4
+STATUS_ZERO_MASS = 5
+STATUS_TOKEN_OUT_OF_RANGE = 6
+STATUS_INVALID_UNIFORM = 7
 STATUS_OVERFLOW = 8
 STATUS_INTERNAL_ERROR = 9
 STATUS_INVALID_SCALE = 10
@@ -40,16 +44,37 @@ FAULT_BLOCK_RANGE = 0x08
 FAULT_CONTEXT_RANGE = 0x10
 FAULT_WAIT_TIMEOUT = 0x20
 FAULT_TABLE_RANGE = 0x40
+FAULT_NEGATIVE_WEIGHT = 0x80
+FAULT_ZERO_MASS = 0x100
+FAULT_TOKEN_RANGE = 0x200
+FAULT_INVALID_UNIFORM = 0x400
+FAULT_PROPOSAL_COUNT = 0x800
 
 FAULT_NAMES = {
-    FAULT_NONFINITE_VALUE: "non-finite KV value",
+    FAULT_NONFINITE_VALUE: "non-finite value",
     FAULT_INVALID_SCALE: "quantization scale outside float32",
     FAULT_SLOT_RANGE: "slot outside the page pool",
     FAULT_BLOCK_RANGE: "block id outside the page pool",
     FAULT_CONTEXT_RANGE: "context length outside the block table",
     FAULT_WAIT_TIMEOUT: "a pipeline wait gave up",
     FAULT_TABLE_RANGE: "block-table edit outside the table",
+    FAULT_NEGATIVE_WEIGHT: "negative probability",
+    FAULT_ZERO_MASS: "zero probability mass",
+    FAULT_TOKEN_RANGE: "token out of range",
+    FAULT_INVALID_UNIFORM: "uniform must be finite and in [0, 1)",
+    FAULT_PROPOSAL_COUNT: "proposal count outside [1, proposals]",
 }
+
+# The reference's status for the input a sampling fault bit reports, in the
+# order its functions check (native/src/native.cpp:29-41, 113-118, 209-225).
+FAULT_STATUS = (
+    (FAULT_INVALID_UNIFORM, STATUS_INVALID_UNIFORM),
+    (FAULT_TOKEN_RANGE, STATUS_TOKEN_OUT_OF_RANGE),
+    (FAULT_NONFINITE_VALUE, STATUS_NONFINITE_VALUE),
+    (FAULT_NEGATIVE_WEIGHT, STATUS_NEGATIVE_PROBABILITY),
+    (FAULT_ZERO_MASS, STATUS_ZERO_MASS),
+    (FAULT_PROPOSAL_COUNT, STATUS_INVALID_SIZE),
+)
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -68,6 +93,12 @@ EXPORTED_SYMBOLS = (
     "sdc_paged_verify_attention",
     "sdc_gather_dequantize",
     "sdc_paged_verify_attention_no_alloc",
+    "sdc_normalize_rows",
+    "sdc_sample_categorical_rows",
+    "sdc_residual_weights_rows",
+    "sdc_acceptance_probabilities_rows",
+    "sdc_first_rejection_rows",
+    "sdc_speculative_verify",
 )
 
 
@@ -114,6 +145,27 @@ class TableEdits(ctypes.Structure):
         ("num_entries", ctypes.c_int64),
         ("lengths", ctypes.c_void_p),
         ("num_lengths", ctypes.c_int64),
+    ]
+
+
+class VerifyBatch(ctypes.Structure):
+    _fields_ = [
+        ("target_rows", ctypes.c_void_p),
+        ("draft_rows", ctypes.c_void_p),
+        ("dtype", ctypes.c_int),
+        ("sequences", ctypes.c_int64),
+        ("proposals", ctypes.c_int64),
+        ("vocab", ctypes.c_int64),
+        ("target_sequence_stride", ctypes.c_int64),
+        ("target_row_stride", ctypes.c_int64),
+        ("draft_sequence_stride", ctypes.c_int64),
+        ("draft_row_stride", ctypes.c_int64),
+        ("proposed_tokens", ctypes.c_void_p),
+        ("token_stride", ctypes.c_int64),
+        ("uniforms", ctypes.c_void_p),
+        ("uniform_stride", ctypes.c_int64),
+        ("proposal_counts", ctypes.c_void_p),
+        ("bonus_allowed", ctypes.c_void_p),
     ]
 
 
@@ -188,6 +240,18 @@ class CudaLibrary:
         h.sdc_gather_dequantize.argtypes = [
             ctypes.POINTER(PagePool), i64, i64, vp, i64, vp, vp, ctypes.c_int, i64, i64, i64, vp, u]
         h.sdc_gather_dequantize.restype = ctypes.c_int
+        h.sdc_normalize_rows.argtypes = [vp, ctypes.c_int, i64, i64, i64, vp, i64, vp, u]
+        h.sdc_normalize_rows.restype = ctypes.c_int
+        h.sdc_sample_categorical_rows.argtypes = [vp, ctypes.c_int, i64, i64, i64, vp, vp, vp, u]
+        h.sdc_sample_categorical_rows.restype = ctypes.c_int
+        h.sdc_residual_weights_rows.argtypes = [vp, vp, ctypes.c_int, i64, i64, i64, i64, vp, i64, vp, u]
+        h.sdc_residual_weights_rows.restype = ctypes.c_int
+        h.sdc_acceptance_probabilities_rows.argtypes = [vp, vp, ctypes.c_int, i64, i64, i64, i64, vp, vp, vp, u]
+        h.sdc_acceptance_probabilities_rows.restype = ctypes.c_int
+        h.sdc_first_rejection_rows.argtypes = [vp, vp, i64, i64, i64, vp, vp, u]
+        h.sdc_first_rejection_rows.restype = ctypes.c_int
+        h.sdc_speculative_verify.argtypes = [ctypes.POINTER(VerifyBatch), vp, vp, vp, vp, u]
+        h.sdc_speculative_verify.restype = ctypes.c_int
 
     def status_string(self, status: int) -> str:
         raw = self.handle.sdc_status_string(int(status))

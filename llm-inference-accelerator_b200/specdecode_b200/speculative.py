@@ -14,8 +14,19 @@ rebuild a legacy cache from the paged mirror on every forward
 models reading and writing their own device page pools through the
 attention hook (``hf_attention``): kernel (a) appends each layer's new keys
 and values, kernel (c) attends over the pool, kernel (b) rolls back the
-rejected tail, and sampling stays on the device (one device-to-host read of
-the round's accepted counts and tokens per round).
+rejected tail, and sampling stays on the device: the draft's tokens come
+from the categorical-sampling kernel and the round's acceptance, first
+rejection and correction or bonus sample from ``sdc_speculative_verify``
+(``sampling.verify_batch``), with one device-to-host read of the round's
+accepted counts and tokens per round.
+
+Draw order.  Each sequence's round takes its uniforms from one row of 2k + 1
+float64 draws of the decoder's device generator, in the reference's order
+(docs/native.md:58-73 of the reference): draws 0 .. k-1 sample the k draft
+tokens, draw k + i decides proposal i, and the draw after the last one used
+samples the correction or the bonus.  The generator is torch's, not the
+reference's ``random.Random``, so token streams are not the reference's; the
+per-sequence decisions given the same draws are (tests/test_gpu_sampling.py).
 
 Cache convention: every committed token but the last is in both caches.  A
 round feeds the draft ``last, d_1 .. d_k`` one token at a time (sampling
@@ -38,6 +49,7 @@ from typing import Hashable, Sequence
 
 from .hf_attention import PagedAttentionSession
 from .kv_cache import PagedKVCache
+from .sampling import raise_for_status, sample_rows, verify_batch
 
 
 @dataclass
@@ -89,34 +101,6 @@ def _distribution(logits, temperature: float):
     return torch.softmax(logits.float() / temperature, dim=-1)
 
 
-def accept_sampled(drafts, draft_probs, target_probs, generator):
-    """The reference's acceptance rule for a batch of windows.
-
-    ``drafts`` int64 ``[B, k]`` were sampled from ``draft_probs [B, k, V]``;
-    ``target_probs [B, k + 1, V]`` are the target's distributions at the same
-    positions plus the bonus position.  Proposal i is accepted with
-    probability ``min(1, q_i(d_i) / p_i(d_i))`` until the first rejection,
-    which is replaced by a sample of ``max(0, q_j - p_j)`` normalised; a fully
-    accepted window adds a sample of ``q_{k+1}``.  Returns the accepted
-    counts ``[B]`` and the round's final token ``[B, 1]``."""
-    import torch
-
-    B, k = drafts.shape
-    q_d = target_probs[:, :k].gather(2, drafts[:, :, None]).squeeze(2)
-    p_d = draft_probs.gather(2, drafts[:, :, None]).squeeze(2)
-    ratio = torch.where(p_d > 0, q_d / p_d, torch.ones_like(q_d))
-    u = torch.rand((B, k), generator=generator, device=drafts.device)
-    ok = u < torch.clamp(ratio, max=1.0)
-    accepted = torch.cumprod(ok.int(), dim=1).sum(dim=1)
-    idx = accepted[:, None, None].expand(B, 1, target_probs.shape[-1])
-    q_j = target_probs.gather(1, idx).squeeze(1)
-    p_full = torch.cat([draft_probs, torch.zeros_like(draft_probs[:, :1])], dim=1)
-    p_j = p_full.gather(1, idx).squeeze(1)
-    resid = torch.clamp(q_j - p_j, min=0.0)
-    weights = torch.where(resid.sum(dim=-1, keepdim=True) > 0, resid, q_j)
-    return accepted, torch.multinomial(weights, 1, generator=generator)
-
-
 def accept_greedy(drafts, target_logits):
     """Greedy verification: proposals are accepted while they equal the
     target's argmax; the final token is the target's argmax after them."""
@@ -165,6 +149,7 @@ class BatchedSpeculativeDecoder:
         self._seen: set = set()
         self._bound = 0
         self._batch = 0
+        self._sampling_status = None
         for model in (draft_model, target_model):
             model.set_attn_implementation(PagedAttentionSession.NAME)
 
@@ -304,6 +289,11 @@ class BatchedSpeculativeDecoder:
         feed = last
         proposals, draft_probs = [], []
         forward = self._graphed_forward if self.cuda_graphs else self._forward
+        if not greedy:
+            # the round's draws: k draft samples, then k + 1 for verification
+            draws = torch.rand((B, 2 * k + 1), generator=gen, device=last.device, dtype=torch.float64)
+            if self._sampling_status is None or self._sampling_status.device != last.device:
+                self._sampling_status = torch.zeros(1, dtype=torch.int32, device=last.device)
         for i in range(k + 1):
             logits = forward(self.draft, self.draft_model, ids, feed, 1)[:, -1]
             if i == k:
@@ -312,7 +302,7 @@ class BatchedSpeculativeDecoder:
                 tok = logits.argmax(dim=-1, keepdim=True)
             else:
                 p = _distribution(logits, self.temperature)
-                tok = torch.multinomial(p, 1, generator=gen)
+                tok = sample_rows(p, draws[:, i], status=self._sampling_status)[:, None]
                 draft_probs.append(p)
             proposals.append(tok)
             feed = tok
@@ -323,11 +313,15 @@ class BatchedSpeculativeDecoder:
         if greedy:
             accepted, new_tok = accept_greedy(drafts, tlogits)
         else:
-            accepted, new_tok = accept_sampled(drafts, torch.stack(draft_probs, dim=1),
-                                               _distribution(tlogits, self.temperature), gen)
+            accepted, token, _ = verify_batch(_distribution(tlogits, self.temperature),
+                                              torch.stack(draft_probs, dim=1), drafts, draws[:, k:],
+                                              status=self._sampling_status)
+            new_tok = token[:, None]
         host = torch.cat([accepted[:, None], drafts, new_tok], dim=1).cpu().tolist()
         self.draft.cache.check_status()
         self.target.cache.check_status()
+        if not greedy:
+            raise_for_status(self._sampling_status, "speculative sampling")
         keep_d, keep_t = [], []
         for b, row in enumerate(host):
             j = int(row[0])

@@ -43,7 +43,7 @@ def test_no_undeclared_sdc_symbols_are_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.handle.sdc_abi_version() == _lib.ABI_VERSION == 0x00020001
+    assert lib.handle.sdc_abi_version() == _lib.ABI_VERSION == 0x00020002
     assert lib.status_string(0) == "ok"
     assert lib.status_string(3) == "non-finite value"
     assert lib.status_string(10) == "invalid quantization scale"
@@ -83,3 +83,36 @@ def test_workspace_sizing_is_host_only(lib):
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(_lib.NativeLibraryNotFound):
         _lib.load_library(tmp_path / "does-not-exist.so")
+
+
+def test_sampling_entry_points_validate_on_the_host(lib):
+    """Null pointers, sizes, dtypes and strides are refused before any launch."""
+    h = lib.handle
+    buf = ctypes.c_void_p(16)  # never dereferenced: every call below fails validation first
+    assert h.sdc_sample_categorical_rows(None, _lib.DTYPE_F64, 1, 4, 4, buf, buf, None, 0) == \
+        _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_sample_categorical_rows(buf, _lib.DTYPE_BF16, 1, 4, 4, buf, buf, None, 0) == \
+        _lib.STATUS_UNSUPPORTED
+    assert h.sdc_sample_categorical_rows(buf, _lib.DTYPE_F64, 0, 4, 4, buf, buf, None, 0) == \
+        _lib.STATUS_INVALID_SIZE
+    assert h.sdc_sample_categorical_rows(buf, _lib.DTYPE_F64, 1, 4, 3, buf, buf, None, 0) == \
+        _lib.STATUS_INVALID_SIZE
+    assert h.sdc_sample_categorical_rows(buf, _lib.DTYPE_F64, 1, (1 << 21) + 1, 1 << 22, buf, buf, None, 0) == \
+        _lib.STATUS_UNSUPPORTED
+    assert h.sdc_normalize_rows(buf, _lib.DTYPE_F32, 2, 8, 8, None, 8, None, 0) == _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_residual_weights_rows(buf, None, _lib.DTYPE_F32, 2, 8, 8, 8, buf, 8, None, 0) == \
+        _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_acceptance_probabilities_rows(buf, buf, _lib.DTYPE_F32, 2, 8, 8, 8, None, buf, None, 0) == \
+        _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_first_rejection_rows(buf, buf, 0, 4, 4, buf, None, 0) == _lib.STATUS_INVALID_SIZE
+    assert h.sdc_first_rejection_rows(buf, buf, 2, 4, 3, buf, None, 0) == _lib.STATUS_INVALID_SIZE
+    out = ctypes.c_void_p(16)
+    assert h.sdc_speculative_verify(None, out, out, out, None, 0) == _lib.STATUS_NULL_ARGUMENT
+    # target sequence stride too small for proposals + 1 rows
+    batch = _lib.VerifyBatch(16, 16, _lib.DTYPE_F32, 2, 3, 100, 300, 100, 300, 100, 16, 3, 16, 4, None, None)
+    assert h.sdc_speculative_verify(ctypes.byref(batch), out, out, out, None, 0) == _lib.STATUS_INVALID_SIZE
+    # uniform stride must hold proposals + 1 draws
+    batch = _lib.VerifyBatch(16, 16, _lib.DTYPE_F32, 2, 3, 100, 400, 100, 300, 100, 16, 3, 16, 3, None, None)
+    assert h.sdc_speculative_verify(ctypes.byref(batch), out, out, out, None, 0) == _lib.STATUS_INVALID_SIZE
+    assert lib.status_string(_lib.STATUS_INVALID_UNIFORM) == "uniform must be finite and in [0, 1)"
+    assert lib.status_string(_lib.STATUS_ZERO_MASS) == "zero probability mass"

@@ -1,46 +1,53 @@
-"""Host-side logic of the batched speculative decoder, on CPU tensors: the
+"""Host-side logic of the batched speculative decoder on CPU: the
 acceptance / resampling rule of the reference decoder
-(src/specdecode/decoder.py:202-257) and its adaptive window
+(src/specdecode/decoder.py:202-257), as the oracle restates it and the
+device verification follows it (tests/test_gpu_sampling.py holds the device
+to the oracle's decisions), greedy verification, and the adaptive window
 (src/specdecode/decoder.py:47-60)."""
 
 from __future__ import annotations
 
+import random
+
+import numpy as np
 import torch
 
-from specdecode_b200.speculative import DraftWindow, accept_greedy, accept_sampled
+from oracle import sampling as orc
+from specdecode_b200.speculative import DraftWindow, accept_greedy
 
 
-def _dists(gen, n, k, V, sharp):
-    return torch.softmax(torch.randn((n, k, V), generator=gen) * sharp, dim=-1)
+def _row(rng, V):
+    p = rng.gamma(0.7, 1.0, V)
+    return tuple(float(x) for x in p / p.sum())
 
 
 def test_identical_distributions_accept_everything():
-    gen = torch.Generator().manual_seed(0)
-    p = _dists(gen, 64, 4, 11, 2.0)
-    q = torch.cat([p, _dists(gen, 64, 1, 11, 2.0)], dim=1)
-    drafts = torch.multinomial(p.reshape(-1, 11), 1, generator=gen).reshape(64, 4)
-    accepted, tok = accept_sampled(drafts, p, q, gen)
-    assert torch.equal(accepted, torch.full((64,), 4))
-    assert tok.shape == (64, 1)
+    rng = np.random.default_rng(0)
+    draws = random.Random(0)
+    for _ in range(50):
+        target = [_row(rng, 11) for _ in range(5)]
+        proposed = [orc.sample_categorical(target[i], draws.random()) for i in range(4)]
+        got = orc.verify_round(target, target[:4], proposed, [draws.random() for _ in range(5)])
+        assert got.accepted == 4 and got.draws == 5 and 0 <= got.token < 11
 
 
 def test_committed_tokens_follow_the_target():
     """Speculative sampling is exact: the first committed token (an accepted
     first proposal or the resampled replacement) is distributed as the
-    target's first distribution, and the token committed after an accepted
-    first proposal as the target's second."""
-    gen = torch.Generator().manual_seed(1)
-    V, k, n = 7, 3, 200_000
-    p1 = torch.softmax(torch.randn(V, generator=gen) * 2, dim=-1)
-    q1 = torch.softmax(torch.randn(V, generator=gen) * 2, dim=-1)
-    p = torch.cat([p1[None], _dists(gen, 1, k - 1, V, 2.0)[0]])[None].expand(n, k, V)
-    q = torch.cat([q1[None], _dists(gen, 1, k, V, 2.0)[0]])[None].expand(n, k + 1, V)
-    drafts = torch.stack([torch.multinomial(p[0, i], n, replacement=True, generator=gen) for i in range(k)], dim=1)
-    accepted, tok = accept_sampled(drafts, p.contiguous(), q.contiguous(), gen)
-    first = torch.where(accepted > 0, drafts[:, 0], tok[:, 0])
-    freq = torch.bincount(first, minlength=V).double() / n
-    assert float((freq - q1.double()).abs().max()) < 0.006
-    assert float(0.5 * (p1 - q1).abs().sum()) > 0.1  # the draft's own distribution is far off
+    target's first distribution, although the draft's is far from it."""
+    rng = np.random.default_rng(1)
+    V, k, n = 5, 2, 12_000
+    target = [_row(rng, V) for _ in range(k + 1)]
+    draft = [_row(rng, V) for _ in range(k)]
+    assert 0.5 * sum(abs(a - b) for a, b in zip(target[0], draft[0])) > 0.1
+    draws = random.Random(2)
+    counts = [0] * V
+    for _ in range(n):
+        proposed = [orc.sample_categorical(draft[i], draws.random()) for i in range(k)]
+        got = orc.verify_round(target, draft, proposed, [draws.random() for _ in range(k + 1)])
+        counts[proposed[0] if got.accepted > 0 else got.token] += 1
+    freq = np.array(counts) / n
+    assert float(np.abs(freq - np.array(target[0])).max()) < 0.02
 
 
 def test_greedy_verification():
