@@ -78,6 +78,10 @@ def parse_args(argv=None):
     p.add_argument("--profile-append", action="store_true",
                    help="the append workload's step (256 sequences x 5 tokens, 32 layers) on a 4096-block pool, "
                         "a few steps, no timing: small enough for a full ncu capture")
+    p.add_argument("--skip-sampling", action="store_true",
+                   help="skip the device acceptance/sampling workload (64 sequences x 6 proposals x 128256 tokens)")
+    p.add_argument("--profile-sampling", action="store_true",
+                   help="the acceptance/sampling workload only, a few rounds, no timing: for ncu")
     p.add_argument("--profile", action="store_true",
                    help="verify attention only: no clock sampling, sustained load, host-buffer pass, append "
                         "workload or CPU baseline (a short, repeatable run for ncu)")
@@ -599,6 +603,98 @@ def profile_append(seed: int, device, steps: int) -> None:
     print(json.dumps({"profile_append": True, "steps": steps}))
 
 
+SAMPLING = {"sequences": 64, "proposals": 6, "vocab": 128256}
+
+
+def sampling_inputs(seed: int, device):
+    """One verification round of the speculative workload's shape: float32
+    softmax rows of the target (proposals + 1 per sequence) and of a draft
+    whose logits are the target's plus N(0, 0.5) noise, proposals drawn from
+    the draft, float64 uniforms."""
+    import torch
+
+    S, k, V = SAMPLING["sequences"], SAMPLING["proposals"], SAMPLING["vocab"]
+    g = torch.Generator(device=device).manual_seed(seed + 7)
+    logits = torch.randn((S, k + 1, V), generator=g, device=device) * 2.0
+    target = torch.softmax(logits, dim=-1)
+    draft = torch.softmax(logits[:, :k] + 0.5 * torch.randn((S, k, V), generator=g, device=device), dim=-1)
+    tokens = torch.multinomial(draft.reshape(-1, V), 1, generator=g).view(S, k)
+    uniforms = torch.rand((S, 2 * k + 1), generator=g, device=device, dtype=torch.float64)
+    return target, draft, tokens, uniforms
+
+
+def run_sampling(seed: int, device, steps: int, warmup: int, profile_only: bool = False):
+    """Device acceptance and sampling at the speculative workload's shape:
+    ``sdc_speculative_verify`` (acceptance probabilities of 64 x 6 proposals
+    over 128 256 tokens, first rejection, correction or bonus sample) and the
+    draft step's ``sdc_sample_categorical_rows`` over 64 rows.  Device time
+    per call; the algorithmic bytes are every row each launch must read."""
+    import torch
+
+    from specdecode_b200.sampling import sample_rows, verify_batch
+
+    target, draft, tokens, uniforms = sampling_inputs(seed, device)
+    S, k, V = SAMPLING["sequences"], SAMPLING["proposals"], SAMPLING["vocab"]
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    draft_rows = target[:, 0].contiguous()
+
+    def verify():
+        return verify_batch(target, draft, tokens, uniforms[:, k:], status=status)
+
+    def sample():
+        return sample_rows(draft_rows, uniforms[:, 0], status=status)
+
+    if profile_only:
+        for _ in range(steps + warmup):
+            verify()
+            sample()
+        torch.cuda.synchronize()
+        if int(status.item()):
+            raise RuntimeError("device fault in the sampling profile run")
+        print(json.dumps({"profile_sampling": True, "rounds": steps + warmup}))
+        return None
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # the Python wrappers take longer to launch than these kernels run:
+        # hold the stream long enough (0.3 ms per call) for the host to queue
+        # every timed call before the start event executes
+        torch.cuda._sleep(HOLD_CYCLES * 3 * steps)
+        start.record()
+        for _ in range(steps):
+            out = fn()
+        end.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / steps, out
+
+    v_ms, (accepted, _, _) = timed(verify)
+    s_ms, _ = timed(sample)
+    if int(status.item()):
+        raise RuntimeError(f"device fault bits 0x{int(status.item()):x} in the sampling workload")
+    acc = accepted.cpu()
+    rejected = int((acc < k).sum())
+    # acceptance launch: every target and draft row of the proposals; the
+    # deciding launch: the rejected pair of rows, or the bonus row
+    v_bytes = 2 * k * S * V * 4 + (2 * rejected + (S - rejected)) * V * 4
+    s_bytes = S * V * 4
+    peak, peak_kind = measured_peaks()
+    return {
+        "workload": f"{S} sequences x {k} proposals, vocab {V}, float32 softmax rows",
+        "verify_us": v_ms * 1e3,
+        "verify_gbs": v_bytes / (v_ms / 1e3) / 1e9,
+        "verify_frac": v_bytes / (v_ms / 1e3) / 1e9 / peak,
+        "verify_bytes": v_bytes,
+        "mean_accepted": float(acc.double().mean()),
+        "sample_rows_us": s_ms * 1e3,
+        "sample_rows_gbs": s_bytes / (s_ms / 1e3) / 1e9,
+        "peak_gbs": peak,
+        "peak_source": peak_kind,
+    }
+
+
 def run_long_context(seed: int, rank: int, world: int, device, steps: int, warmup: int):
     """Llama-3.1-70B long-context verify, one layer: 8 sequences x 131072
     tokens, 64 query / 8 KV heads, window 5.  KV heads are split over the
@@ -755,6 +851,9 @@ def main(argv=None) -> int:
     if args.profile_append:
         profile_append(args.seed, device, args.steps + args.warmup)
         return 0
+    if args.profile_sampling:
+        run_sampling(args.seed, device, args.steps, args.warmup, profile_only=True)
+        return 0
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
     state = build_verify(args.seed + 1000 * rank, device)
 
@@ -800,6 +899,10 @@ def main(argv=None) -> int:
     if not args.skip_long:
         long_ctx = run_long_context(args.seed, rank, world, device, args.steps, args.warmup)
 
+    sampling = None
+    if not args.skip_sampling:
+        sampling = run_sampling(args.seed + 1000 * rank, device, args.steps, args.warmup)
+
     speculative = None
     if not args.skip_speculative:
         speculative = run_speculative(args.seed + 1000 * rank, device, world)
@@ -839,6 +942,7 @@ def main(argv=None) -> int:
             "gpu_launches": 3 * args.steps,
             "append": append,
             "long_context_70b": long_ctx,
+            "speculative_sampling": sampling,
             "speculative_e2e": speculative,
             "cpu_baseline": cpu,
             "clocks": clocks,

@@ -338,7 +338,10 @@ SDC_API sdc_status_t sdc_first_rejection_rows(
  * or bonus token, or -1 after a full acceptance without a bonus.  A faulted
  * sequence gets -1 in both.  Two launches: one block per (sequence,
  * proposal) for the acceptance probabilities, then one per sequence for the
- * decision and the sample.
+ * decision and the sample.  row_sums (optional, NULL allowed) is device
+ * scratch of sequences * proposals * 4 doubles through which the first
+ * launch hands its row sums to the second, which then reads only the
+ * rejected rows' residual instead of summing both rows again.
  */
 typedef struct sdc_verify_batch {
     const void* target_rows;
@@ -361,7 +364,7 @@ typedef struct sdc_verify_batch {
 
 SDC_API sdc_status_t sdc_speculative_verify(
     const sdc_verify_batch_t* batch, double* output_probabilities, int64_t* output_accepted,
-    int64_t* output_tokens, int32_t* device_status, uintptr_t stream);
+    int64_t* output_tokens, double* row_sums, int32_t* device_status, uintptr_t stream);
 
 #ifdef __cplusplus
 }

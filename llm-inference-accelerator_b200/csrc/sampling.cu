@@ -130,29 +130,82 @@ __device__ __forceinline__ DD warp_exclusive_scan(DD x, int lane) {
 // Weight views and validation.
 // ---------------------------------------------------------------------------
 
-// The reference's per-weight checks (native.cpp:29-34) on the bit pattern,
-// off the double-precision pipe: an all-ones exponent is not finite; a set
-// sign bit on anything but -0 is negative.
-__device__ __forceinline__ int weight_faults(float x) {
-    const uint32_t b = __float_as_uint(x);
-    if ((b & 0x7f800000u) == 0x7f800000u) return SDC_FAULT_NONFINITE_VALUE;
-    return b > 0x80000000u ? SDC_FAULT_NEGATIVE_WEIGHT : 0;
-}
+// The reference's per-weight checks (native.cpp:29-34) on the bit patterns,
+// off the double-precision pipe.  A lane keeps two running maxima: of the
+// magnitude bits (all-ones exponent or more: not finite) and of the raw
+// bits (above the pattern of -0: a set sign bit on a non-zero: negative).
+// Only the high word of a double matters for either test.
+struct WeightCheck {
+    uint32_t mag = 0, raw = 0;
+    __device__ __forceinline__ void add(float x) {
+        const uint32_t b = __float_as_uint(x);
+        mag = max(mag, b & 0x7fffffffu);
+        raw = max(raw, b);
+    }
+    __device__ __forceinline__ void add(double x) {
+        const uint32_t h = static_cast<uint32_t>(static_cast<uint64_t>(__double_as_longlong(x)) >> 32);
+        const uint32_t l = static_cast<uint32_t>(__double_as_longlong(x));
+        // f64 exponent all ones <=> high word magnitude >= 0x7ff00000; a
+        // negative non-zero has a high word above 0x80000000, or exactly
+        // 0x80000000 with a non-zero low word
+        mag = max(mag, (h & 0x7fffffffu) >= 0x7ff00000u ? 0x7f800000u : 0u);
+        raw = max(raw, h > 0x80000000u || (h == 0x80000000u && l != 0) ? 0x80000001u : 0u);
+    }
+    __device__ __forceinline__ int faults() const {
+        if (mag >= 0x7f800000u) return SDC_FAULT_NONFINITE_VALUE;
+        return raw > 0x80000000u ? SDC_FAULT_NEGATIVE_WEIGHT : 0;
+    }
+};
 
-__device__ __forceinline__ int weight_faults(double x) {
-    const uint64_t b = static_cast<uint64_t>(__double_as_longlong(x));
-    if ((b & 0x7ff0000000000000ull) == 0x7ff0000000000000ull) return SDC_FAULT_NONFINITE_VALUE;
-    return b > 0x8000000000000000ull ? SDC_FAULT_NEGATIVE_WEIGHT : 0;
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Weights v0 .. v0 + 3 of a row (v0 a multiple of 4), zero past the
+// vocabulary: one 16-byte load (two for f64) where the row is 16-byte
+// aligned and all four exist, element loads otherwise.
+template <typename T>
+__device__ __forceinline__ void load_quad(const T* row, bool vec, int64_t v0, int64_t vocab, T (&q)[4]) {
+    if (vec && v0 + 3 < vocab) {
+        if constexpr (sizeof(T) == 4) {
+            const float4 f = __ldg(reinterpret_cast<const float4*>(row + v0));
+            q[0] = f.x, q[1] = f.y, q[2] = f.z, q[3] = f.w;
+        } else {
+            const double2 a = __ldg(reinterpret_cast<const double2*>(row + v0));
+            const double2 b = __ldg(reinterpret_cast<const double2*>(row + v0 + 2));
+            q[0] = a.x, q[1] = a.y, q[2] = b.x, q[3] = b.y;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) q[e] = v0 + e < vocab ? row[v0 + e] : T(0);
+    }
 }
 
 template <typename T>
 struct Stored {  // the row as stored
     const T* row;
+    bool vec;
+    __device__ explicit Stored(const T* r) : row(r), vec(aligned16(r)) {}
     __device__ __forceinline__ double operator()(int64_t v) const { return static_cast<double>(row[v]); }
-    __device__ __forceinline__ double load(int64_t v, int& faults) const {
-        const T x = row[v];
-        faults |= weight_faults(x);
-        return static_cast<double>(x);
+    // Raw quads kept in flight: four per lane for f32 rows, two for f64.
+    struct Raw {
+        T q[4];
+    };
+    static constexpr int kDepth = sizeof(T) == 4 ? 4 : 2;
+    __device__ __forceinline__ void load_raw(int64_t v0, int64_t vocab, Raw& r) const {
+        load_quad(row, vec, v0, vocab, r.q);
+    }
+    template <bool Check>
+    __device__ __forceinline__ void convert(const Raw& r, double (&x)[4], WeightCheck& check) const {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (Check) check.add(r.q[e]);
+            x[e] = static_cast<double>(r.q[e]);
+        }
+    }
+    template <bool Check>
+    __device__ __forceinline__ void load4(int64_t v0, int64_t vocab, double (&x)[4], WeightCheck& check) const {
+        Raw r;
+        load_raw(v0, vocab, r);
+        convert<Check>(r, x, check);
     }
 };
 
@@ -166,17 +219,39 @@ struct Residual {
     const T* t;
     const T* d;
     DD inv_t, inv_d;
-    __device__ __forceinline__ double operator()(int64_t v) const {
-        const double x = static_cast<double>(t[v]);
-        const double y = static_cast<double>(d[v]);
+    bool vec_t, vec_d;
+    __device__ Residual(const T* t_, const T* d_, DD it, DD id)
+        : t(t_), d(d_), inv_t(it), inv_d(id), vec_t(aligned16(t_)), vec_d(aligned16(d_)) {}
+    __device__ __forceinline__ double value(double x, double y) const {
         const DD p = two_prod(inv_t.hi, x);
         const DD q = two_prod(inv_d.hi, y);
         const DD s = two_sum(p.hi, -q.hi);
-        const double lo = __fma_rn(inv_t.lo, x, p.lo) - __fma_rn(inv_d.lo, y, q.lo);
+        const double lo = __dsub_rn(__fma_rn(inv_t.lo, x, p.lo), __fma_rn(inv_d.lo, y, q.lo));
         const double r = __dadd_rn(s.hi, __dadd_rn(s.lo, lo));
         return r > 0.0 ? r : 0.0;
     }
-    __device__ __forceinline__ double load(int64_t v, int&) const { return (*this)(v); }
+    __device__ __forceinline__ double operator()(int64_t v) const {
+        return value(static_cast<double>(t[v]), static_cast<double>(d[v]));
+    }
+    struct Raw {
+        T a[4], b[4];
+    };
+    static constexpr int kDepth = 2;
+    __device__ __forceinline__ void load_raw(int64_t v0, int64_t vocab, Raw& r) const {
+        load_quad(t, vec_t, v0, vocab, r.a);
+        load_quad(d, vec_d, v0, vocab, r.b);
+    }
+    template <bool Check>
+    __device__ __forceinline__ void convert(const Raw& r, double (&x)[4], WeightCheck&) const {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = value(static_cast<double>(r.a[e]), static_cast<double>(r.b[e]));
+    }
+    template <bool Check>
+    __device__ __forceinline__ void load4(int64_t v0, int64_t vocab, double (&x)[4], WeightCheck& check) const {
+        Raw r;
+        load_raw(v0, vocab, r);
+        convert<Check>(r, x, check);
+    }
 };
 
 // native.cpp:44-46: a uniform must be finite and in [0, 1).
@@ -198,47 +273,63 @@ struct RowShared {
     int64_t index;
 };
 
+// Compensated sum: sum + comp carries the exact running sum up to the
+// rounding of comp itself -- every addition's exact error (TwoSum, seven
+// additions in all, no comparisons) lands in comp, whose own rounding stays
+// below 2^-99 of the sum for a lane's 128 weights.
+__device__ __forceinline__ void accumulate(double& sum, double& comp, const double (&x)[4]) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const DD s = two_sum(sum, x[e]);
+        comp = __dadd_rn(comp, s.lo);
+        sum = s.hi;
+    }
+}
+
 // Sums the row's tiles into sh.tile[] and their in-order total into
-// sh.total.  With `check`, ORs the weights' faults into the returned word
+// sh.total.  With Check, ORs the weights' faults into the returned word
 // (the same on every thread).  All threads of the block must call it.
-template <class W>
-__device__ int row_sums(const W& w, int64_t vocab, RowShared& sh, bool check) {
+template <bool Check, class W>
+__device__ int row_sums(const W& w, int64_t vocab, RowShared& sh) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles = static_cast<int>((vocab + kTile - 1) / kTile);
     __syncthreads();  // earlier readers of sh are done
     if (threadIdx.x == 0) sh.faults = 0;
     __syncthreads();
-    int faults = 0;
+    WeightCheck check;
+    constexpr int kChunks = kTile / kChunk;
     for (int t = warp; t < tiles; t += kWarps) {
-        // Compensated sum of non-negative weights: s + c carries the exact
-        // running sum up to the rounding of c itself.  With s, x >= 0 the
-        // larger of the two is the Fast2Sum head, so each weight costs one
-        // max, one min and four additions, and the exact error of every
-        // addition lands in c.  (A negative or non-finite weight faults the
-        // row, so its sum is never used.)
-        double sum = 0.0, comp = 0.0;
+        // W::kDepth chunks of raw weights in flight per lane: each slot is
+        // refilled with the chunk kDepth ahead as soon as it is converted;
+        // two chains (even and odd slots) halve the addition latency
+        constexpr int kDepth = W::kDepth;
+        double sum0 = 0.0, comp0 = 0.0, sum1 = 0.0, comp1 = 0.0;
         const int64_t first = static_cast<int64_t>(t) * kTile + lane * 4;
-        for (int c = 0; c < kTile / kChunk; c += 2) {
-            double x[8];
+        typename W::Raw buf[kDepth];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int64_t v = first + static_cast<int64_t>(c + j / 4) * kChunk + (j % 4);
-                x[j] = v < vocab ? (check ? w.load(v, faults) : w(v)) : 0.0;
-            }
+        for (int j = 0; j < kDepth; ++j) w.load_raw(first + static_cast<int64_t>(j) * kChunk, vocab, buf[j]);
+#pragma unroll 1
+        for (int c = 0; c < kChunks; c += kDepth) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const double hi = fmax(sum, x[j]);
-                const double lo = fmin(sum, x[j]);
-                const double next = __dadd_rn(hi, lo);
-                comp = __dadd_rn(comp, __dsub_rn(lo, __dsub_rn(next, hi)));
-                sum = next;
+            for (int j = 0; j < kDepth; ++j) {
+                double x[4];
+                w.template convert<Check>(buf[j], x, check);
+                if (c + kDepth + j < kChunks) {
+                    w.load_raw(first + static_cast<int64_t>(c + kDepth + j) * kChunk, vocab, buf[j]);
+                }
+                if (j % 2 == 0) {
+                    accumulate(sum0, comp0, x);
+                } else {
+                    accumulate(sum1, comp1, x);
+                }
             }
         }
-        DD acc = fast_two_sum(sum, comp);
+        DD acc = dd_add(fast_two_sum(sum0, comp0), fast_two_sum(sum1, comp1));
         acc = warp_sum(acc);
         if (lane == 0) sh.tile[t] = acc;
     }
-    if (check && faults) atomicOr(&sh.faults, faults);
+    const int faults = Check ? check.faults() : 0;
+    if (faults) atomicOr(&sh.faults, faults);
     __syncthreads();
     if (threadIdx.x == 0) {
         DD s{0.0, 0.0};
@@ -277,9 +368,12 @@ __device__ int64_t row_search(const W& w, int64_t vocab, DD thr, RowShared& sh) 
         const int64_t tile_first = static_cast<int64_t>(tile) * kTile;
         {
             const int64_t first = tile_first + warp * kChunk + lane * 4;
+            double x[4];
+            WeightCheck unused;
+            w.template load4<false>(first, vocab, x, unused);
             DD acc{0.0, 0.0};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc = dd_add(acc, first + e < vocab ? w(first + e) : 0.0);
+            for (int e = 0; e < 4; ++e) acc = dd_add(acc, x[e]);
             acc = warp_sum(acc);
             if (lane == 0) sh.chunk[warp] = acc;
         }
@@ -305,12 +399,11 @@ __device__ int64_t row_search(const W& w, int64_t vocab, DD thr, RowShared& sh) 
             const int64_t chunk_first = tile_first + static_cast<int64_t>(sh.pick) * kChunk;
             const int64_t first = chunk_first + lane * 4;
             double x[4];
+            WeightCheck unused;
+            w.template load4<false>(first, vocab, x, unused);
             DD mine{0.0, 0.0};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                x[e] = first + e < vocab ? w(first + e) : 0.0;
-                mine = dd_add(mine, x[e]);
-            }
+            for (int e = 0; e < 4; ++e) mine = dd_add(mine, x[e]);
             DD run = dd_add(sh.base, warp_exclusive_scan(mine, lane));
             int hit = 4;
 #pragma unroll
@@ -345,8 +438,8 @@ __global__ void __launch_bounds__(kThreads) normalize_kernel(const T* weights, i
                                                               double* out, int64_t out_stride, int32_t* status) {
     __shared__ RowShared sh;
     const int64_t r = blockIdx.x;
-    const Stored<T> w{weights + r * stride};
-    int faults = row_sums(w, vocab, sh, true);
+    const Stored<T> w(weights + r * stride);
+    int faults = row_sums<true>(w, vocab, sh);
     if (!(sh.total.hi > 0.0)) faults |= SDC_FAULT_ZERO_MASS;
     if (faults) {
         if (threadIdx.x == 0) report_fault(status, faults);
@@ -362,9 +455,9 @@ __global__ void __launch_bounds__(kThreads) categorical_kernel(const T* weights,
                                                                 int32_t* status) {
     __shared__ RowShared sh;
     const int64_t r = blockIdx.x;
-    const Stored<T> w{weights + r * stride};
+    const Stored<T> w(weights + r * stride);
     const double u = uniforms[r];
-    int faults = row_sums(w, vocab, sh, true) | uniform_faults(u);
+    int faults = row_sums<true>(w, vocab, sh) | uniform_faults(u);
     if (!(sh.total.hi > 0.0)) faults |= SDC_FAULT_ZERO_MASS;
     if (faults) {
         if (threadIdx.x == 0) {
@@ -381,9 +474,9 @@ __global__ void __launch_bounds__(kThreads) categorical_kernel(const T* weights,
 // sums in *st / *sd.
 template <typename T>
 __device__ int pair_sums(const T* t, const T* d, int64_t vocab, RowShared& sh, DD* st, DD* sd) {
-    int faults = row_sums(Stored<T>{t}, vocab, sh, true);
+    int faults = row_sums<true>(Stored<T>(t), vocab, sh);
     *st = sh.total;
-    faults |= row_sums(Stored<T>{d}, vocab, sh, true);
+    faults |= row_sums<true>(Stored<T>(d), vocab, sh);
     *sd = sh.total;
     if (!(st->hi > 0.0) || !(sd->hi > 0.0)) faults |= SDC_FAULT_ZERO_MASS;
     return faults;
@@ -405,8 +498,8 @@ __global__ void __launch_bounds__(kThreads) residual_kernel(const T* target, int
         if (threadIdx.x == 0) report_fault(status, faults);
         return;
     }
-    const Residual<T> res{t, d, reciprocal(st), reciprocal(sd)};
-    row_sums(res, vocab, sh, false);
+    const Residual<T> res(t, d, reciprocal(st), reciprocal(sd));
+    row_sums<false>(res, vocab, sh);
     const bool fallback = !dd_lt(DD{1.0e-15, 0.0}, sh.total);
     double* o = out + r * out_stride;
     if (fallback) {
@@ -432,7 +525,8 @@ struct AcceptArgs {
     const int64_t* tokens;
     int64_t token_stride;
     const int64_t* counts;
-    double* out;  // [sequences][proposals]
+    double* out;   // [sequences][proposals]
+    double* sums;  // [sequences][proposals][4]: S_t, S_d as double-doubles, or null
     int32_t* status;
 };
 
@@ -458,6 +552,10 @@ __global__ void __launch_bounds__(kThreads) acceptance_kernel(AcceptArgs a) {
         return;
     }
     *out = acceptance(static_cast<double>(t[token]), static_cast<double>(d[token]), st, sd);
+    if (a.sums != nullptr) {
+        double* w = a.sums + (s * a.proposals + i) * 4;
+        w[0] = st.hi, w[1] = st.lo, w[2] = sd.hi, w[3] = sd.lo;
+    }
 }
 
 // native.cpp:247-272 for one row of probabilities and uniforms.
@@ -493,6 +591,7 @@ struct ResolveArgs {
     int64_t uniform_stride;
     const int64_t* counts;
     const uint8_t* bonus;
+    const double* sums;  // written by acceptance_kernel, or null
     int64_t* accepted;
     int64_t* tokens;
     int32_t* status;
@@ -529,21 +628,28 @@ __global__ void __launch_bounds__(kThreads) resolve_kernel(ResolveArgs a) {
         const T* t = static_cast<const T*>(a.target) + s * a.t_seq + j * a.t_row;
         const T* d = static_cast<const T*>(a.draft) + s * a.d_seq + j * a.d_row;
         DD st, sd;
-        faults |= pair_sums(t, d, a.vocab, sh, &st, &sd);
+        if (a.sums != nullptr) {
+            // validated, and the row sums formed, by the acceptance launch
+            const double* w = a.sums + (s * a.proposals + j) * 4;
+            st = DD{w[0], w[1]};
+            sd = DD{w[2], w[3]};
+        } else {
+            faults |= pair_sums(t, d, a.vocab, sh, &st, &sd);
+        }
         if (!faults) {
-            const Residual<T> res{t, d, reciprocal(st), reciprocal(sd)};
-            row_sums(res, a.vocab, sh, false);
+            const Residual<T> res(t, d, reciprocal(st), reciprocal(sd));
+            row_sums<false>(res, a.vocab, sh);
             if (dd_lt(DD{1.0e-15, 0.0}, sh.total)) {
                 token = row_search(res, a.vocab, dd_mul(sh.total, u[j + 1]), sh);
             } else {
-                const Stored<T> w{t};
-                row_sums(w, a.vocab, sh, false);
+                const Stored<T> w(t);
+                row_sums<false>(w, a.vocab, sh);
                 token = row_search(w, a.vocab, dd_mul(sh.total, u[j + 1]), sh);
             }
         }
     } else if (!faults && (a.bonus == nullptr || a.bonus[s] != 0)) {
-        const Stored<T> w{static_cast<const T*>(a.target) + s * a.t_seq + n * a.t_row};
-        faults |= row_sums(w, a.vocab, sh, true);
+        const Stored<T> w(static_cast<const T*>(a.target) + s * a.t_seq + n * a.t_row);
+        faults |= row_sums<true>(w, a.vocab, sh);
         if (!(sh.total.hi > 0.0)) faults |= SDC_FAULT_ZERO_MASS;
         if (!faults) token = row_search(w, a.vocab, dd_mul(sh.total, u[n]), sh);
     }
@@ -665,7 +771,7 @@ SDC_API sdc_status_t sdc_acceptance_probabilities_rows(const void* target, const
         if (proposed_tokens == nullptr || output_probabilities == nullptr) return SDC_STATUS_NULL_ARGUMENT;
         // rows independent proposals: `rows` sequences of one proposal each
         AcceptArgs a{target, draft, target_stride, 0, draft_stride, 0, 1, vocab, proposed_tokens, 1,
-                     nullptr, output_probabilities, device_status};
+                     nullptr, output_probabilities, nullptr, device_status};
         const dim3 grid(static_cast<unsigned>(rows), 1);
         if (dtype == SDC_DTYPE_F32) {
             acceptance_kernel<float><<<grid, kThreads, 0, as_stream(stream)>>>(a);
@@ -696,7 +802,7 @@ SDC_API sdc_status_t sdc_first_rejection_rows(const double* acceptance_probabili
 }
 
 SDC_API sdc_status_t sdc_speculative_verify(const sdc_verify_batch_t* batch, double* output_probabilities,
-                                            int64_t* output_accepted, int64_t* output_tokens,
+                                            int64_t* output_accepted, int64_t* output_tokens, double* row_sums,
                                             int32_t* device_status, uintptr_t stream) {
     return guarded([&]() -> sdc_status_t {
         if (batch == nullptr || output_probabilities == nullptr || output_accepted == nullptr ||
@@ -724,10 +830,10 @@ SDC_API sdc_status_t sdc_speculative_verify(const sdc_verify_batch_t* batch, dou
         }
         AcceptArgs a{b.target_rows, b.draft_rows, b.target_sequence_stride, b.target_row_stride,
                      b.draft_sequence_stride, b.draft_row_stride, b.proposals, b.vocab, b.proposed_tokens,
-                     b.token_stride, b.proposal_counts, output_probabilities, device_status};
+                     b.token_stride, b.proposal_counts, output_probabilities, row_sums, device_status};
         ResolveArgs r{b.target_rows, b.draft_rows, b.target_sequence_stride, b.target_row_stride,
                       b.draft_sequence_stride, b.draft_row_stride, b.proposals, b.vocab, output_probabilities,
-                      b.uniforms, b.uniform_stride, b.proposal_counts, b.bonus_allowed, output_accepted,
+                      b.uniforms, b.uniform_stride, b.proposal_counts, b.bonus_allowed, row_sums, output_accepted,
                       output_tokens, device_status};
         const dim3 grid_a(static_cast<unsigned>(b.sequences), static_cast<unsigned>(b.proposals));
         const dim3 grid_r(static_cast<unsigned>(b.sequences));

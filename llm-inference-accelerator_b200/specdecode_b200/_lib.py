@@ -250,7 +250,7 @@ class CudaLibrary:
         h.sdc_acceptance_probabilities_rows.restype = ctypes.c_int
         h.sdc_first_rejection_rows.argtypes = [vp, vp, i64, i64, i64, vp, vp, u]
         h.sdc_first_rejection_rows.restype = ctypes.c_int
-        h.sdc_speculative_verify.argtypes = [ctypes.POINTER(VerifyBatch), vp, vp, vp, vp, u]
+        h.sdc_speculative_verify.argtypes = [ctypes.POINTER(VerifyBatch), vp, vp, vp, vp, vp, u]
         h.sdc_speculative_verify.restype = ctypes.c_int
 
     def status_string(self, status: int) -> str:

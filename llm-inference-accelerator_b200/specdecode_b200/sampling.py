@@ -196,7 +196,7 @@ def first_rejection_rows(probabilities, uniforms, *, status=None, library=None):
 
 
 def verify_batch(target, draft, tokens, uniforms, *, proposal_counts=None, bonus_allowed=None, status=None,
-                 out_accepted=None, out_tokens=None, out_probabilities=None, library=None):
+                 out_accepted=None, out_tokens=None, out_probabilities=None, reuse_row_sums=True, library=None):
     """One verification round for every sequence of a batch.
 
     ``target`` [S, k + 1, V] and ``draft`` [S, k, V] (float32 or float64, unit
@@ -211,7 +211,9 @@ def verify_batch(target, draft, tokens, uniforms, *, proposal_counts=None, bonus
 
     Returns (accepted [S] int64, token [S] int64, probabilities [S, k]
     float64); token is the correction or bonus, -1 after a full acceptance
-    without a bonus; a faulted sequence gets -1 in both."""
+    without a bonus; a faulted sequence gets -1 in both.  With
+    ``reuse_row_sums`` the deciding launch takes the row sums from the first
+    through a small scratch tensor instead of summing the rows again."""
     import torch
 
     lib = _library(library)
@@ -249,6 +251,7 @@ def verify_batch(target, draft, tokens, uniforms, *, proposal_counts=None, bonus
     probs = out_probabilities if out_probabilities is not None else torch.empty((S, k), dtype=torch.float64,
                                                                                   device=dev)
     st = _status(status, dev)
+    sums = torch.empty((S, k, 4), dtype=torch.float64, device=dev) if reuse_row_sums else None
     t_row = target.stride(1)
     d_row = _stride(draft, 1, V)
     batch = _lib.VerifyBatch(
@@ -256,7 +259,8 @@ def verify_batch(target, draft, tokens, uniforms, *, proposal_counts=None, bonus
         _stride(draft, 0, k * d_row), d_row, tok.data_ptr(), _stride(tok, 0, k), u.data_ptr(),
         _stride(u, 0, u.shape[1]),
         counts.data_ptr() if counts is not None else None, bonus.data_ptr() if bonus is not None else None)
-    lib.check(lib.handle.sdc_speculative_verify(ctypes.byref(batch), probs.data_ptr(), accepted.data_ptr(), final.data_ptr(),
+    lib.check(lib.handle.sdc_speculative_verify(ctypes.byref(batch), probs.data_ptr(), accepted.data_ptr(),
+                                                final.data_ptr(), sums.data_ptr() if sums is not None else None,
                                                 st.data_ptr(), _stream(dev)),
               "speculative verification")
     return accepted, final, probs

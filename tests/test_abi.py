@@ -107,12 +107,12 @@ def test_sampling_entry_points_validate_on_the_host(lib):
     assert h.sdc_first_rejection_rows(buf, buf, 0, 4, 4, buf, None, 0) == _lib.STATUS_INVALID_SIZE
     assert h.sdc_first_rejection_rows(buf, buf, 2, 4, 3, buf, None, 0) == _lib.STATUS_INVALID_SIZE
     out = ctypes.c_void_p(16)
-    assert h.sdc_speculative_verify(None, out, out, out, None, 0) == _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_speculative_verify(None, out, out, out, None, None, 0) == _lib.STATUS_NULL_ARGUMENT
     # target sequence stride too small for proposals + 1 rows
     batch = _lib.VerifyBatch(16, 16, _lib.DTYPE_F32, 2, 3, 100, 300, 100, 300, 100, 16, 3, 16, 4, None, None)
-    assert h.sdc_speculative_verify(ctypes.byref(batch), out, out, out, None, 0) == _lib.STATUS_INVALID_SIZE
+    assert h.sdc_speculative_verify(ctypes.byref(batch), out, out, out, None, None, 0) == _lib.STATUS_INVALID_SIZE
     # uniform stride must hold proposals + 1 draws
     batch = _lib.VerifyBatch(16, 16, _lib.DTYPE_F32, 2, 3, 100, 400, 100, 300, 100, 16, 3, 16, 3, None, None)
-    assert h.sdc_speculative_verify(ctypes.byref(batch), out, out, out, None, 0) == _lib.STATUS_INVALID_SIZE
+    assert h.sdc_speculative_verify(ctypes.byref(batch), out, out, out, None, None, 0) == _lib.STATUS_INVALID_SIZE
     assert lib.status_string(_lib.STATUS_INVALID_UNIFORM) == "uniform must be finite and in [0, 1)"
     assert lib.status_string(_lib.STATUS_ZERO_MASS) == "zero probability mass"

@@ -105,9 +105,9 @@ def test_verify_round_matches_the_reference_decoder(device, record):
     variants = [dict(normalised=True), dict(normalised=False)]
     if case.name.startswith(("softmax", "near", "identical", "v1")):
         variants.append(dict(normalised=False, dtype=torch.float32))  # rows exact in float32
-    for v in variants:
+    for v, reuse in [(v, r) for v in variants for r in (True, False)]:
         t, d, tok, u = _round_inputs(device, case, **v)
-        acc, token, probs = verify_batch(t, d, tok, u, bonus_allowed=bonus, status=status)
+        acc, token, probs = verify_batch(t, d, tok, u, bonus_allowed=bonus, status=status, reuse_row_sums=reuse)
         assert (int(acc.item()), int(token.item())) == (want["accepted"], want["token"]), v
         if v["normalised"]:
             assert within_ulps(probs[0].cpu().numpy(), want["probabilities"]), v
