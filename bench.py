@@ -392,6 +392,11 @@ def run_speculative(seed: int, device, world: int):
     from specdecode_b200.speculative import BatchedSpeculativeDecoder, DraftWindow
 
     sp = SPEC
+    # start from an empty allocator cache: the earlier workloads leave large
+    # cached blocks behind, and the decoding loop's own large tensors (the
+    # rounds' probability rows) must not have to evict them mid-run
+    gc.collect()
+    torch.cuda.empty_cache()
     torch.manual_seed(seed)
     draft = _random_llama(sp["draft"], sp["vocab"], device)
     target = _random_llama(sp["target"], sp["vocab"], device)
