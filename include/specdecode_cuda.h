@@ -78,6 +78,8 @@ typedef enum sdc_status {
 #define SDC_FAULT_TOKEN_RANGE      0x200  /* a proposed token outside the vocabulary [6] */
 #define SDC_FAULT_INVALID_UNIFORM  0x400  /* a uniform outside [0, 1) [7] */
 #define SDC_FAULT_PROPOSAL_COUNT   0x800  /* a proposal count outside [1, proposals] */
+/* Device page allocator. */
+#define SDC_FAULT_CAPACITY         0x1000 /* an append needs more free blocks than the pool has */
 
 typedef enum sdc_dtype {
     SDC_DTYPE_F32 = 0,
@@ -365,6 +367,83 @@ typedef struct sdc_verify_batch {
 SDC_API sdc_status_t sdc_speculative_verify(
     const sdc_verify_batch_t* batch, double* output_probabilities, int64_t* output_accepted,
     int64_t* output_tokens, double* row_sums, int32_t* device_status, uintptr_t stream);
+
+/*
+ * Device-resident page allocation: the reference's lowest-free-block-first
+ * allocator (the min-heap of src/specdecode/kv_cache.py:220-221, :327, :418,
+ * whose order the block tables follow exactly) held on the device, so append
+ * and rollback plan their blocks without a host round trip; plus prefix
+ * sharing -- a forked sequence shares its source's blocks, reference-counted
+ * -- with copy-on-write of a shared, partly filled last block on the next
+ * append.  The reference defers sharing (docs/kv-cache.md:105-108); the
+ * sharing semantics are this library's own.
+ *
+ * State, all device memory the caller owns: free_bits (bit h % 32 of word
+ * h / 32 set = heap id h free; bits past num_blocks clear), refcount per
+ * physical block (0 when free), block_order (heap id -> physical block) and
+ * heap_of (its inverse), the block tables (-1 = no block) and the context
+ * lengths.  Rows passed to one call must be distinct.  A call that fails
+ * validation on the device sets a fault bit and changes nothing.
+ */
+typedef struct sdc_page_allocator {
+    uint32_t* free_bits;
+    int32_t* refcount;
+    const int32_t* block_order;
+    const int32_t* heap_of;
+    int32_t* block_tables;
+    int32_t* context_lens;
+    int64_t num_blocks;
+    int64_t block_size;
+    int64_t table_rows;
+    int64_t table_stride;
+} sdc_page_allocator_t;
+
+/* Workspace bytes of sdc_pages_append for this many sequences (1 .. 1024) and tokens. */
+SDC_API sdc_status_t sdc_pages_append_workspace_size(
+    int64_t sequences, int64_t total_tokens, int64_t block_size, size_t* bytes);
+
+/*
+ * Reserves room for counts[s] more tokens in table row rows[s] (device int32
+ * arrays of `sequences` entries, total_tokens = their sum) and writes the
+ * physical slot of every new token to slot_mapping (int64, sequence order
+ * then token order), ready for sdc_quantize_append.  New blocks are the
+ * lowest free heap ids, taken in sequence order; a shared partly filled last
+ * block is first copied (rows below the old length; the rest zeroed) into a
+ * private block.  Faults: SDC_FAULT_CAPACITY (the pool is short of blocks),
+ * SDC_FAULT_TABLE_RANGE (a row out of range, a table row too short, counts
+ * not summing to total_tokens); a faulted call changes no state and sets
+ * every slot to -1, which sdc_quantize_append refuses to write.
+ * Replaces PagedKVCache.append_many's block allocation (src/specdecode/kv_cache.py:298-336).
+ */
+SDC_API sdc_status_t sdc_pages_append(
+    const sdc_page_allocator_t* allocator, const sdc_page_pool_t* pool, const int32_t* rows,
+    const int32_t* counts, int64_t sequences, int64_t total_tokens, int64_t* slot_mapping,
+    void* workspace, size_t workspace_bytes, int32_t* device_status, uintptr_t stream);
+
+/*
+ * Truncates table row rows[s] to new_lengths[s] tokens (device int32
+ * arrays; at most max_removed tokens removed from any row): blocks past the
+ * new length drop a reference and return to the free set when none is left,
+ * their pages zeroed whole; in a partly kept last page held by this row
+ * alone the rows at or past the new length are zeroed (codes and scales of
+ * every layer and head), as the reference's rollback leaves released slots.
+ * Faults: SDC_FAULT_CONTEXT_RANGE (a new length above the old one or more
+ * than max_removed below it; that row is left unchanged).
+ * Replaces PagedKVCache.truncate / rollback (src/specdecode/kv_cache.py:382-420).
+ */
+SDC_API sdc_status_t sdc_pages_truncate(
+    const sdc_page_allocator_t* allocator, const sdc_page_pool_t* pool, const int32_t* rows,
+    const int32_t* new_lengths, int64_t sequences, int64_t max_removed, int32_t* device_status,
+    uintptr_t stream);
+
+/*
+ * Prefix sharing: destination_rows[i] (empty) takes every block and the
+ * length of source_rows[i]; each shared block gains a reference.  No
+ * counterpart in the reference.
+ */
+SDC_API sdc_status_t sdc_pages_fork(
+    const sdc_page_allocator_t* allocator, const int32_t* source_rows, const int32_t* destination_rows,
+    int64_t pairs, int32_t* device_status, uintptr_t stream);
 
 #ifdef __cplusplus
 }

@@ -49,6 +49,7 @@ FAULT_ZERO_MASS = 0x100
 FAULT_TOKEN_RANGE = 0x200
 FAULT_INVALID_UNIFORM = 0x400
 FAULT_PROPOSAL_COUNT = 0x800
+FAULT_CAPACITY = 0x1000
 
 FAULT_NAMES = {
     FAULT_NONFINITE_VALUE: "non-finite value",
@@ -63,6 +64,7 @@ FAULT_NAMES = {
     FAULT_TOKEN_RANGE: "token out of range",
     FAULT_INVALID_UNIFORM: "uniform must be finite and in [0, 1)",
     FAULT_PROPOSAL_COUNT: "proposal count outside [1, proposals]",
+    FAULT_CAPACITY: "the page pool is short of free blocks",
 }
 
 # The reference's status for the input a sampling fault bit reports, in the
@@ -99,6 +101,10 @@ EXPORTED_SYMBOLS = (
     "sdc_acceptance_probabilities_rows",
     "sdc_first_rejection_rows",
     "sdc_speculative_verify",
+    "sdc_pages_append_workspace_size",
+    "sdc_pages_append",
+    "sdc_pages_truncate",
+    "sdc_pages_fork",
 )
 
 
@@ -166,6 +172,21 @@ class VerifyBatch(ctypes.Structure):
         ("uniform_stride", ctypes.c_int64),
         ("proposal_counts", ctypes.c_void_p),
         ("bonus_allowed", ctypes.c_void_p),
+    ]
+
+
+class PageAllocator(ctypes.Structure):
+    _fields_ = [
+        ("free_bits", ctypes.c_void_p),
+        ("refcount", ctypes.c_void_p),
+        ("block_order", ctypes.c_void_p),
+        ("heap_of", ctypes.c_void_p),
+        ("block_tables", ctypes.c_void_p),
+        ("context_lens", ctypes.c_void_p),
+        ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int64),
+        ("table_rows", ctypes.c_int64),
+        ("table_stride", ctypes.c_int64),
     ]
 
 
@@ -252,6 +273,16 @@ class CudaLibrary:
         h.sdc_first_rejection_rows.restype = ctypes.c_int
         h.sdc_speculative_verify.argtypes = [ctypes.POINTER(VerifyBatch), vp, vp, vp, vp, vp, u]
         h.sdc_speculative_verify.restype = ctypes.c_int
+        h.sdc_pages_append_workspace_size.argtypes = [i64, i64, i64, ctypes.POINTER(ctypes.c_size_t)]
+        h.sdc_pages_append_workspace_size.restype = ctypes.c_int
+        h.sdc_pages_append.argtypes = [ctypes.POINTER(PageAllocator), ctypes.POINTER(PagePool), vp, vp, i64, i64, vp,
+                                       vp, ctypes.c_size_t, vp, u]
+        h.sdc_pages_append.restype = ctypes.c_int
+        h.sdc_pages_truncate.argtypes = [ctypes.POINTER(PageAllocator), ctypes.POINTER(PagePool), vp, vp, i64, i64,
+                                         vp, u]
+        h.sdc_pages_truncate.restype = ctypes.c_int
+        h.sdc_pages_fork.argtypes = [ctypes.POINTER(PageAllocator), vp, vp, i64, vp, u]
+        h.sdc_pages_fork.restype = ctypes.c_int
 
     def status_string(self, status: int) -> str:
         raw = self.handle.sdc_status_string(int(status))
