@@ -78,6 +78,8 @@ def parse_args(argv=None):
     p.add_argument("--profile-append", action="store_true",
                    help="the append workload's step (256 sequences x 5 tokens, 32 layers) on a 4096-block pool, "
                         "a few steps, no timing: small enough for a full ncu capture")
+    p.add_argument("--skip-device-pages", action="store_true",
+                   help="skip the append workload's step through the device-resident page allocator")
     p.add_argument("--skip-sampling", action="store_true",
                    help="skip the device acceptance/sampling workload (64 sequences x 6 proposals x 128256 tokens)")
     p.add_argument("--profile-sampling", action="store_true",
@@ -608,6 +610,66 @@ def profile_append(seed: int, device, steps: int) -> None:
     print(json.dumps({"profile_append": True, "steps": steps}))
 
 
+def run_device_pages(seed: int, device, steps: int, warmup: int, world: int):
+    """The append workload's speculative step (256 sequences append 5 tokens
+    to 32 layers x 8 heads, then roll back 0-5 of them) with the block tables,
+    lengths and free set on the device (DevicePagedCache): planning is a
+    kernel, so the step is kernel launches only.  Wall-clock step rate through
+    the Python API (as the append workload's api_step_tokens_per_s) and the
+    step's device time."""
+    import numpy as np
+    import torch
+
+    from specdecode_b200.device_pages import DevicePagedCache
+    from specdecode_b200.kv_cache import KVCacheConfig
+
+    a = APPEND
+    rng = np.random.default_rng(seed + 1)
+    cache = DevicePagedCache(KVCacheConfig(a["layers"], a["kv_heads"], a["head_dim"], block_size=a["block_size"],
+                                           num_blocks=a["num_blocks"]),
+                             max_rows=a["sequences"], max_blocks_per_row=512,
+                             block_order=rng.permutation(a["num_blocks"]), device=device)
+    rows = list(range(a["sequences"]))
+    gen = torch.Generator(device=device).manual_seed(seed + 2)
+    shape = (a["sequences"], a["window"], a["layers"], a["kv_heads"], a["head_dim"])
+    keys = torch.randn(shape, generator=gen, device=device).to(torch.bfloat16)
+    values = torch.randn(shape, generator=gen, device=device).to(torch.bfloat16)
+    rolled = rng.integers(0, a["window"] + 1, size=(warmup + 2 * steps, a["sequences"]))
+
+    def step(i):
+        cache.append(rows, keys, values)
+        cache.truncate(rows, [int(cache.length_bound[r]) - int(k) for r, k in zip(rows, rolled[i])])
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    for i in range(warmup, warmup + steps):
+        step(i)
+    torch.cuda.synchronize()
+    host_s = time.perf_counter() - h0
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(HOLD_CYCLES * 5 * steps)  # the host queues every step before the start event runs
+    start.record()
+    for i in range(warmup + steps, warmup + 2 * steps):
+        step(i)
+    end.record()
+    torch.cuda.synchronize()
+    device_ms = start.elapsed_time(end) / steps
+    cache.check_status()
+    cache.validate_invariants()
+    tokens = a["sequences"] * a["window"]
+    del cache, keys, values
+    torch.cuda.empty_cache()
+    return {
+        "workload": "256 sequences x 5 tokens appended then 0-5 rolled back per step, 32 layers x 8 heads x 128, "
+                    "65536 blocks of 16, permuted block order; tables, lengths and free set on the device",
+        "api_step_tokens_per_s": sum_over_ranks(tokens * steps, world) / max_over_ranks(host_s, world),
+        "device_ms_per_step": max_over_ranks(device_ms, world),
+        "device_step_tokens_per_s": sum_over_ranks(tokens, world) / (max_over_ranks(device_ms, world) / 1e3),
+    }
+
+
 SAMPLING = {"sequences": 64, "proposals": 6, "vocab": 128256}
 
 
@@ -904,6 +966,10 @@ def main(argv=None) -> int:
     if not args.skip_long:
         long_ctx = run_long_context(args.seed, rank, world, device, args.steps, args.warmup)
 
+    device_pages = None
+    if not args.skip_device_pages:
+        device_pages = run_device_pages(args.seed + 1000 * rank, device, args.steps, args.warmup, world)
+
     sampling = None
     if not args.skip_sampling:
         sampling = run_sampling(args.seed + 1000 * rank, device, args.steps, args.warmup)
@@ -947,6 +1013,7 @@ def main(argv=None) -> int:
             "gpu_launches": 3 * args.steps,
             "append": append,
             "long_context_70b": long_ctx,
+            "device_pages": device_pages,
             "speculative_sampling": sampling,
             "speculative_e2e": speculative,
             "cpu_baseline": cpu,

@@ -425,8 +425,8 @@ SDC_API sdc_status_t sdc_pages_append(
  * arrays; at most max_removed tokens removed from any row): blocks past the
  * new length drop a reference and return to the free set when none is left,
  * their pages zeroed whole; in a partly kept last page held by this row
- * alone the rows at or past the new length are zeroed (codes and scales of
- * every layer and head), as the reference's rollback leaves released slots.
+ * alone the removed rows are zeroed (codes and scales of every layer and
+ * head), as the reference's rollback leaves released slots.
  * Faults: SDC_FAULT_CONTEXT_RANGE (a new length above the old one or more
  * than max_removed below it; that row is left unchanged).
  * Replaces PagedKVCache.truncate / rollback (src/specdecode/kv_cache.py:382-420).

@@ -205,39 +205,44 @@ __global__ void __launch_bounds__(kPlanThreads) append_plan_kernel(AppendPlanArg
     }
 }
 
-// Copy-on-write: block (s, layer) copies the kept rows of the shared page
-// (every head, keys and values, codes and scales) into the fresh page and
-// zeroes the rest, so a page's slots beyond its sequence's length hold zeros.
+// Rows [first, last) of one page (every layer and head, keys and values,
+// codes and scales) in page `to`: rows below `keep` copied from page `from`,
+// the others zeroed (from < 0 zeroes them all).  In a page the rows of one
+// (layer, key|value, head) are contiguous, so each such span is one run of
+// 16-byte stores; warps take spans in turn, lanes the run's chunks.
+__device__ void page_rows(const Pool& pool, int32_t from, int32_t to, int64_t first, int64_t last,
+                          int64_t keep) {
+    if (last <= first) return;
+    const int64_t D = pool.head_dim, H = pool.num_heads, L = pool.num_layers;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    const int64_t copy_end = from >= 0 ? max(first, min(keep, last)) : first;
+    for (int64_t sp = warp; sp < 2 * L * H; sp += warps) {
+        const bool value_side = sp >= L * H;
+        const int64_t lh = value_side ? sp - L * H : sp;
+        const int64_t layer = lh / H, head = lh - layer * H;
+        int8_t* codes = (value_side ? pool.values : pool.keys) + layer * pool.cls + head * pool.chs;
+        float* scales = (value_side ? pool.value_scales : pool.key_scales) + layer * pool.sls + head * pool.shs;
+        if (copy_end > first) {
+            const uint4* src = reinterpret_cast<const uint4*>(codes + from * pool.cbs + first * D);
+            uint4* dst = reinterpret_cast<uint4*>(codes + to * pool.cbs + first * D);
+            for (int64_t c = lane; c < (copy_end - first) * D / 16; c += 32) dst[c] = src[c];
+            for (int64_t r = first + lane; r < copy_end; r += 32) scales[to * pool.sbs + r] = scales[from * pool.sbs + r];
+        }
+        uint4* dst = reinterpret_cast<uint4*>(codes + to * pool.cbs + copy_end * D);
+        for (int64_t c = lane; c < (last - copy_end) * D / 16; c += 32) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+        for (int64_t r = copy_end + lane; r < last; r += 32) scales[to * pool.sbs + r] = 0.0f;
+    }
+}
+
+// Copy-on-write: block s copies the kept rows of sequence s's shared page
+// into its fresh page and zeroes the rest, so a page's slots beyond its
+// sequence's length hold zeros.  Sequences without a copy return at once.
 __global__ void __launch_bounds__(kCopyThreads) page_copy_kernel(Pool pool, const int32_t* copies) {
     const int32_t* c = copies + static_cast<int64_t>(blockIdx.x) * 4;
     const int32_t from = c[0];
     const int32_t to = c[1];
     if (from < 0 || from >= pool.num_blocks || to < 0 || to >= pool.num_blocks) return;
-    const int64_t keep = c[2];
-    const int64_t layer = blockIdx.y;
-    const int64_t D = pool.head_dim, bs = pool.block_size, H = pool.num_heads;
-    const int64_t row_chunks = D / 16;
-    const int64_t chunks = 2 * H * bs * row_chunks;
-    for (int64_t i = threadIdx.x; i < chunks; i += blockDim.x) {
-        const int64_t kv_head = i / (bs * row_chunks);
-        const int64_t rest = i - kv_head * bs * row_chunks;
-        const int64_t off = rest / row_chunks, ch = rest - off * row_chunks;
-        const bool value_side = kv_head >= H;
-        const int64_t head = value_side ? kv_head - H : kv_head;
-        int8_t* base = value_side ? pool.values : pool.keys;
-        const int64_t rel = layer * pool.cls + head * pool.chs + off * D + ch * 16;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (off < keep) v = *reinterpret_cast<const uint4*>(base + from * pool.cbs + rel);
-        *reinterpret_cast<uint4*>(base + to * pool.cbs + rel) = v;
-    }
-    for (int64_t i = threadIdx.x; i < 2 * H * bs; i += blockDim.x) {
-        const int64_t kv_head = i / bs, off = i - kv_head * bs;
-        const bool value_side = kv_head >= H;
-        const int64_t head = value_side ? kv_head - H : kv_head;
-        float* base = value_side ? pool.value_scales : pool.key_scales;
-        const int64_t rel = layer * pool.sls + head * pool.shs + off;
-        base[to * pool.sbs + rel] = off < keep ? base[from * pool.sbs + rel] : 0.0f;
-    }
+    page_rows(pool, from, to, 0, pool.block_size, c[2]);
 }
 
 struct TruncateArgs {
@@ -263,11 +268,11 @@ __device__ __forceinline__ bool truncate_valid(const TruncateArgs& t, int s, int
 //   1. truncate_mark_kernel (a thread per row): drops one reference from
 //      every block past the new length; a block whose last reference goes
 //      is marked -1 (released in this call) instead of 0;
-//   2. truncate_zero_kernel (a block per row, page and layer): zeroes a
-//      released page's every row, and the rows at or past the new length of
-//      the partly kept last page when this row alone holds it (a shared
-//      page's rows still belong to the other rows), so freed pages and
-//      released slots hold zeros as the reference's rollback leaves them;
+//   2. truncate_zero_kernel (a block per row and page): zeroes a released
+//      page's every row, and the removed rows of the partly kept last page
+//      when this row alone holds it (a shared page's rows still belong to
+//      the other rows), so freed pages and released slots hold zeros as the
+//      reference's rollback leaves them;
 //   3. truncate_finish_kernel (a thread per row): returns the marked blocks
 //      to the free set (the first row to claim a block does it), clears the
 //      table entries and sets the length.
@@ -302,37 +307,12 @@ __global__ void __launch_bounds__(kCopyThreads) truncate_zero_kernel(TruncateArg
     if (b >= blocks_for(old, a.block_size)) return;
     const int32_t blk = a.tables[row * a.stride + b];
     if (blk < 0 || blk >= a.num_blocks) return;
-    const bool kept = b < blocks_for(now, a.block_size);  // the partly kept last page
-    int64_t first;
-    if (kept) {
+    if (b < blocks_for(now, a.block_size)) {
+        // the partly kept last page: the removed rows, when this row alone holds it
         if (a.refcount[blk] != 1) return;
-        first = now % a.block_size;
-    } else {
-        if (a.refcount[blk] != -1) return;
-        first = 0;
-    }
-    const Pool& pool = t.pool;
-    const int64_t D = pool.head_dim, H = pool.num_heads, bs = pool.block_size;
-    const int64_t layer = blockIdx.z;
-    const int64_t row_chunks = D / 16;
-    const int64_t rows = bs - first;
-    const int64_t chunks = 2 * H * rows * row_chunks;
-    for (int64_t i = threadIdx.x; i < chunks; i += blockDim.x) {
-        const int64_t kv_head = i / (rows * row_chunks);
-        const int64_t rest = i - kv_head * rows * row_chunks;
-        const int64_t off = first + rest / row_chunks, ch = rest % row_chunks;
-        const bool value_side = kv_head >= H;
-        const int64_t head = value_side ? kv_head - H : kv_head;
-        int8_t* base = value_side ? pool.values : pool.keys;
-        *reinterpret_cast<uint4*>(base + blk * pool.cbs + layer * pool.cls + head * pool.chs + off * D + ch * 16) =
-            make_uint4(0u, 0u, 0u, 0u);
-    }
-    for (int64_t i = threadIdx.x; i < 2 * H * rows; i += blockDim.x) {
-        const int64_t kv_head = i / rows, off = first + i % rows;
-        const bool value_side = kv_head >= H;
-        const int64_t head = value_side ? kv_head - H : kv_head;
-        float* base = value_side ? pool.value_scales : pool.key_scales;
-        base[blk * pool.sbs + layer * pool.sls + head * pool.shs + off] = 0.0f;
+        page_rows(t.pool, -1, blk, now % a.block_size, min(a.block_size, old - b * a.block_size), 0);
+    } else if (a.refcount[blk] == -1) {
+        page_rows(t.pool, -1, blk, 0, a.block_size, 0);  // released in this call: the whole page
     }
 }
 
@@ -456,8 +436,7 @@ SDC_API sdc_status_t sdc_pages_append(const sdc_page_allocator_t* allocator, con
                          device_status};
         cudaStream_t s = as_stream(stream);
         append_plan_kernel<<<1, kPlanThreads, 0, s>>>(p);
-        page_copy_kernel<<<dim3(static_cast<unsigned>(sequences), static_cast<unsigned>(pool->num_layers)),
-                           kCopyThreads, 0, s>>>(to_pool(pool), copies);
+        page_copy_kernel<<<static_cast<unsigned>(sequences), kCopyThreads, 0, s>>>(to_pool(pool), copies);
         return launch_status();
     });
 }
@@ -482,8 +461,7 @@ SDC_API sdc_status_t sdc_pages_truncate(const sdc_page_allocator_t* allocator, c
         if (max_removed > 0) {
             // pages a truncation of at most max_removed tokens touches
             const int64_t pages = (max_removed + a.block_size - 1) / a.block_size + 1;
-            truncate_zero_kernel<<<dim3(static_cast<unsigned>(sequences), static_cast<unsigned>(pages),
-                                        static_cast<unsigned>(pool->num_layers)),
+            truncate_zero_kernel<<<dim3(static_cast<unsigned>(sequences), static_cast<unsigned>(pages)),
                                    kCopyThreads, 0, s>>>(t);
         }
         truncate_finish_kernel<<<row_blocks, kPlanThreads, 0, s>>>(t);

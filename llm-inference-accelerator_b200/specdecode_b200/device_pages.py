@@ -14,8 +14,9 @@ no host-to-device table copies:
   ``PagedKVCache``); ``append`` then quantizes into the reserved slots with
   kernel (a);
 * ``truncate`` / ``release``: blocks past the new length return to the free
-  set, and unshared rows at or past it are zeroed, as the reference's
-  rollback leaves released slots;
+  set with their pages zeroed, and the removed rows of an unshared, partly
+  kept last page are zeroed, as the reference's rollback leaves released
+  slots;
 * ``fork``: prefix sharing, which the reference defers
   (docs/kv-cache.md:105-108): an empty row takes another row's blocks and
   length, each block reference-counted, and the first append into a shared,
@@ -42,6 +43,38 @@ def _torch():
     import torch
 
     return torch
+
+
+class _Staging:
+    """Pinned host rows for the small per-call arrays (rows, counts,
+    lengths), copied to the device asynchronously.  A pageable copy would
+    wait for the stream to drain; a ring of pinned slots lets the host queue
+    many calls ahead.  A slot is reused only after its copy has run."""
+
+    def __init__(self, device, width: int, depth: int = 64) -> None:
+        torch = _torch()
+        self.host = torch.empty((depth, 2, width), dtype=torch.int32, pin_memory=True)
+        self.dev = torch.empty((depth, 2, width), dtype=torch.int32, device=device)
+        self.events = [None] * depth
+        self.next = 0
+        self.device = device
+
+    def put(self, first: Sequence[int], second: Sequence[int] | None = None):
+        torch = _torch()
+        k = self.next
+        self.next = (k + 1) % len(self.events)
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        n = len(first)
+        view = self.host[k].numpy()
+        view[0, :n] = first
+        if second is not None:
+            view[1, :n] = second
+        self.dev[k, :, :n].copy_(self.host[k, :, :n], non_blocking=True)
+        event = torch.cuda.Event()
+        event.record(torch.cuda.current_stream(self.device))
+        self.events[k] = event
+        return self.dev[k, 0, :n], self.dev[k, 1, :n]
 
 
 class DevicePagedCache:
@@ -95,6 +128,7 @@ class DevicePagedCache:
             max_rows, stride)
         self.length_bound = np.zeros(max_rows, dtype=np.int64)
         self._workspace = torch.empty(0, dtype=torch.uint8, device=dev)
+        self._staging = _Staging(dev, max(max_rows, 1))
 
     @property
     def library(self) -> _lib.CudaLibrary:
@@ -107,7 +141,7 @@ class DevicePagedCache:
     def _stream(self) -> int:
         return _torch().cuda.current_stream(self.device).cuda_stream
 
-    def _rows(self, rows: Sequence[int], *, distinct: bool = True):
+    def _rows(self, rows: Sequence[int], *, distinct: bool = True) -> list[int]:
         rows = [int(r) for r in rows]
         if not rows:
             raise ValueError("at least one row is required")
@@ -115,8 +149,7 @@ class DevicePagedCache:
             raise ValueError("rows must be distinct")
         if min(rows) < 0 or max(rows) >= self.max_rows:
             raise IndexError("row outside the table")
-        torch = _torch()
-        return rows, torch.tensor(rows, dtype=torch.int32, device=self.device)
+        return rows
 
     # -- status -----------------------------------------------------------------
     def status_bits(self, *, reset: bool = True) -> int:
@@ -142,7 +175,7 @@ class DevicePagedCache:
         """Room for counts[i] more tokens in each of ``rows``; returns the
         slots of the new tokens (device int64, row order then token order)."""
         torch = _torch()
-        rows, rows_t = self._rows(rows)
+        rows = self._rows(rows)
         counts = [int(c) for c in counts]
         if len(counts) != len(rows) or min(counts) < 0:
             raise ValueError("one non-negative count per row is required")
@@ -155,7 +188,7 @@ class DevicePagedCache:
         if self._workspace.numel() < size.value:
             self._workspace = torch.empty(max(size.value, 1 << 16), dtype=torch.uint8, device=self.device)
         slots = torch.empty(total, dtype=torch.int64, device=self.device)
-        counts_t = torch.tensor(counts, dtype=torch.int32, device=self.device)
+        rows_t, counts_t = self._staging.put(rows, counts)
         self._lib.check(self._lib.handle.sdc_pages_append(
             self.allocator_desc, self.pool_desc, rows_t.data_ptr(), counts_t.data_ptr(), len(rows), total,
             slots.data_ptr() if total else None, self._workspace.data_ptr(), self._workspace.numel(),
@@ -185,13 +218,12 @@ class DevicePagedCache:
 
     def truncate(self, rows: Sequence[int], new_lengths: Sequence[int]) -> None:
         """Rolls ``rows`` back to ``new_lengths`` tokens."""
-        torch = _torch()
-        rows, rows_t = self._rows(rows)
+        rows = self._rows(rows)
         lengths = [int(n) for n in new_lengths]
         if len(lengths) != len(rows) or min(lengths) < 0:
             raise ValueError("one non-negative length per row is required")
         removed = max(max(int(self.length_bound[r]) - n, 0) for r, n in zip(rows, lengths))
-        lengths_t = torch.tensor(lengths, dtype=torch.int32, device=self.device)
+        rows_t, lengths_t = self._staging.put(rows, lengths)
         self._lib.check(self._lib.handle.sdc_pages_truncate(
             self.allocator_desc, self.pool_desc, rows_t.data_ptr(), lengths_t.data_ptr(), len(rows), removed,
             self._status.data_ptr(), self._stream()), "page truncation")
@@ -207,10 +239,11 @@ class DevicePagedCache:
     def fork(self, sources: Sequence[int], destinations: Sequence[int]) -> None:
         """Each (empty) destination row shares its source row's blocks; a
         source may be forked more than once."""
-        src, src_t = self._rows(sources, distinct=False)
-        dst, dst_t = self._rows(destinations)
+        src = self._rows(sources, distinct=False)
+        dst = self._rows(destinations)
         if len(src) != len(dst) or set(src) & set(dst):
             raise ValueError("sources and destinations must pair up and be different rows")
+        src_t, dst_t = self._staging.put(src, dst)
         self._lib.check(self._lib.handle.sdc_pages_fork(
             self.allocator_desc, src_t.data_ptr(), dst_t.data_ptr(), len(src), self._status.data_ptr(),
             self._stream()), "page fork")
