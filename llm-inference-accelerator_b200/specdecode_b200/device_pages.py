@@ -138,6 +138,19 @@ class DevicePagedCache:
     def max_rows(self) -> int:
         return int(self.block_tables.shape[0])
 
+    @property
+    def status(self):
+        """The device fault word (int32 [1]) every call of this cache ORs into."""
+        return self._status
+
+    def attention(self):
+        """Kernel (c) over this pool: ``attention(query, block_tables,
+        context_lens, max_context_len, layer)`` with rows of this cache's
+        tables and lengths."""
+        from .cuda_kv_cache import PagedVerifyAttention
+
+        return PagedVerifyAttention(self.pool_desc, self.device, self._lib, self._status)
+
     def _stream(self) -> int:
         return _torch().cuda.current_stream(self.device).cuda_stream
 

@@ -93,11 +93,10 @@ def test_tables_and_pool_follow_the_reference_allocator(device, permuted):
 
     # attention over the device tables and lengths
     from oracle.attention import attention_fp64
-    from specdecode_b200.cuda_kv_cache import PagedVerifyAttention
 
     live = [r for r in range(R) if oracle.sequence_length(r) >= 2]
     if live:
-        attention = PagedVerifyAttention(cache.pool_desc, device, cache.library, cache._status)
+        attention = cache.attention()
         q = torch.randn((len(live), 4, 2, D), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
         idx = torch.tensor(live, device=device)
         out = attention(q.to(device), cache.block_tables[idx].contiguous(), cache.context_lens[idx].contiguous(),
