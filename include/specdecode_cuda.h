@@ -380,7 +380,9 @@ SDC_API sdc_status_t sdc_speculative_verify(
  *
  * State, all device memory the caller owns: free_bits (bit h % 32 of word
  * h / 32 set = heap id h free; bits past num_blocks clear), refcount per
- * physical block (0 when free), block_order (heap id -> physical block) and
+ * physical block (0 when free), high_water per physical block (rows
+ * [0, high_water) of the page may be non-zero; 0 initially), block_order
+ * (heap id -> physical block) and
  * heap_of (its inverse), the block tables (-1 = no block) and the context
  * lengths.  Rows passed to one call must be distinct.  A call that fails
  * validation on the device sets a fault bit and changes nothing.
@@ -388,6 +390,7 @@ SDC_API sdc_status_t sdc_speculative_verify(
 typedef struct sdc_page_allocator {
     uint32_t* free_bits;
     int32_t* refcount;
+    int32_t* high_water;
     const int32_t* block_order;
     const int32_t* heap_of;
     int32_t* block_tables;
@@ -424,9 +427,9 @@ SDC_API sdc_status_t sdc_pages_append(
  * Truncates table row rows[s] to new_lengths[s] tokens (device int32
  * arrays; at most max_removed tokens removed from any row): blocks past the
  * new length drop a reference and return to the free set when none is left,
- * their pages zeroed whole; in a partly kept last page held by this row
- * alone the removed rows are zeroed (codes and scales of every layer and
- * head), as the reference's rollback leaves released slots.
+ * their written rows zeroed; in a partly kept last page held by this row
+ * alone the rows past the new length are zeroed (codes and scales of every
+ * layer and head), as the reference's rollback leaves released slots.
  * Faults: SDC_FAULT_CONTEXT_RANGE (a new length above the old one or more
  * than max_removed below it; that row is left unchanged).
  * Replaces PagedKVCache.truncate / rollback (src/specdecode/kv_cache.py:382-420).

@@ -30,6 +30,7 @@ constexpr int kCopyThreads = 256;
 struct Alloc {
     uint32_t* free_bits;
     int32_t* refcount;
+    int32_t* high_water;  // per physical block: rows [0, high_water) may be non-zero
     const int32_t* block_order;
     const int32_t* heap_of;
     int32_t* tables;
@@ -171,6 +172,7 @@ __global__ void __launch_bounds__(kPlanThreads) append_plan_kernel(AppendPlanArg
                 const int32_t fresh = a.block_order[heap];
                 table[old / a.block_size] = fresh;
                 a.refcount[fresh] = 1;
+                a.high_water[fresh] = static_cast<int32_t>(old % a.block_size);
                 copy[1] = fresh;
                 copy[2] = static_cast<int32_t>(old % a.block_size);
                 copy[0] = shared;
@@ -202,6 +204,7 @@ __global__ void __launch_bounds__(kPlanThreads) append_plan_kernel(AppendPlanArg
         const int32_t r = p.rows[lo];
         const int64_t blk = a.tables[r * a.stride + pos / a.block_size];
         p.slots[i] = blk * a.block_size + pos % a.block_size;
+        atomicMax(a.high_water + blk, static_cast<int32_t>(pos % a.block_size) + 1);
     }
 }
 
@@ -213,24 +216,33 @@ __global__ void __launch_bounds__(kPlanThreads) append_plan_kernel(AppendPlanArg
 __device__ void page_rows(const Pool& pool, int32_t from, int32_t to, int64_t first, int64_t last,
                           int64_t keep) {
     if (last <= first) return;
-    const int64_t D = pool.head_dim, H = pool.num_heads, L = pool.num_layers;
+    const int64_t D = pool.head_dim;
+    const int H = static_cast<int>(pool.num_heads), L = static_cast<int>(pool.num_layers);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
     const int64_t copy_end = from >= 0 ? max(first, min(keep, last)) : first;
-    for (int64_t sp = warp; sp < 2 * L * H; sp += warps) {
-        const bool value_side = sp >= L * H;
-        const int64_t lh = value_side ? sp - L * H : sp;
-        const int64_t layer = lh / H, head = lh - layer * H;
-        int8_t* codes = (value_side ? pool.values : pool.keys) + layer * pool.cls + head * pool.chs;
-        float* scales = (value_side ? pool.value_scales : pool.key_scales) + layer * pool.sls + head * pool.shs;
-        if (copy_end > first) {
-            const uint4* src = reinterpret_cast<const uint4*>(codes + from * pool.cbs + first * D);
-            uint4* dst = reinterpret_cast<uint4*>(codes + to * pool.cbs + first * D);
-            for (int64_t c = lane; c < (copy_end - first) * D / 16; c += 32) dst[c] = src[c];
-            for (int64_t r = first + lane; r < copy_end; r += 32) scales[to * pool.sbs + r] = scales[from * pool.sbs + r];
+    const int copy_chunks = static_cast<int>((copy_end - first) * D / 16);
+    const int zero_chunks = static_cast<int>((last - copy_end) * D / 16);
+    // spans in (layer, key|value, head) order without divisions: the warp
+    // walks its heads of every layer
+    for (int layer = 0; layer < L; ++layer) {
+        for (int kvh = warp; kvh < 2 * H; kvh += warps) {
+            const bool value_side = kvh >= H;
+            const int head = value_side ? kvh - H : kvh;
+            int8_t* codes = (value_side ? pool.values : pool.keys) + layer * pool.cls + head * pool.chs;
+            float* scales =
+                (value_side ? pool.value_scales : pool.key_scales) + layer * pool.sls + head * pool.shs;
+            if (copy_chunks > 0) {
+                const uint4* src = reinterpret_cast<const uint4*>(codes + from * pool.cbs + first * D);
+                uint4* dst = reinterpret_cast<uint4*>(codes + to * pool.cbs + first * D);
+                for (int c = lane; c < copy_chunks; c += 32) dst[c] = src[c];
+                for (int64_t r = first + lane; r < copy_end; r += 32) {
+                    scales[to * pool.sbs + r] = scales[from * pool.sbs + r];
+                }
+            }
+            uint4* dst = reinterpret_cast<uint4*>(codes + to * pool.cbs + copy_end * D);
+            for (int c = lane; c < zero_chunks; c += 32) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+            for (int64_t r = copy_end + lane; r < last; r += 32) scales[to * pool.sbs + r] = 0.0f;
         }
-        uint4* dst = reinterpret_cast<uint4*>(codes + to * pool.cbs + copy_end * D);
-        for (int64_t c = lane; c < (last - copy_end) * D / 16; c += 32) dst[c] = make_uint4(0u, 0u, 0u, 0u);
-        for (int64_t r = copy_end + lane; r < last; r += 32) scales[to * pool.sbs + r] = 0.0f;
     }
 }
 
@@ -264,15 +276,16 @@ __device__ __forceinline__ bool truncate_valid(const TruncateArgs& t, int s, int
 }
 
 // Truncation runs in three launches so that pages released by several rows
-// of one call are found free exactly once and zeroed whole:
+// of one call are found free exactly once and zeroed:
 //   1. truncate_mark_kernel (a thread per row): drops one reference from
 //      every block past the new length; a block whose last reference goes
 //      is marked -1 (released in this call) instead of 0;
 //   2. truncate_zero_kernel (a block per row and page): zeroes a released
-//      page's every row, and the removed rows of the partly kept last page
-//      when this row alone holds it (a shared page's rows still belong to
-//      the other rows), so freed pages and released slots hold zeros as the
-//      reference's rollback leaves them;
+//      page's written rows, and the rows past the new length of the partly
+//      kept last page when this row alone holds it (a shared page's rows
+//      still belong to the other rows) -- up to the page's high-water mark,
+//      the rows any holder has written -- so freed pages and slots past a
+//      length hold zeros, as the reference's rollback leaves them;
 //   3. truncate_finish_kernel (a thread per row): returns the marked blocks
 //      to the free set (the first row to claim a block does it), clears the
 //      table entries and sets the length.
@@ -307,13 +320,27 @@ __global__ void __launch_bounds__(kCopyThreads) truncate_zero_kernel(TruncateArg
     if (b >= blocks_for(old, a.block_size)) return;
     const int32_t blk = a.tables[row * a.stride + b];
     if (blk < 0 || blk >= a.num_blocks) return;
+    __shared__ int32_t s_high;
+    int64_t first;
     if (b < blocks_for(now, a.block_size)) {
-        // the partly kept last page: the removed rows, when this row alone holds it
+        // the partly kept last page: its rows past the new length, when this row alone holds it
         if (a.refcount[blk] != 1) return;
-        page_rows(t.pool, -1, blk, now % a.block_size, min(a.block_size, old - b * a.block_size), 0);
+        first = now % a.block_size;
     } else if (a.refcount[blk] == -1) {
-        page_rows(t.pool, -1, blk, 0, a.block_size, 0);  // released in this call: the whole page
+        first = 0;  // released in this call: every written row
+    } else {
+        return;
     }
+    // rows at or past `first` that may hold data: up to the page's high water,
+    // read once so that every thread of the block zeroes the same rows (a
+    // page released by several rows has several blocks; whichever resets the
+    // mark has zeroed the rows first)
+    if (threadIdx.x == 0) s_high = a.high_water[blk];
+    __syncthreads();
+    const int64_t high = s_high;
+    page_rows(t.pool, -1, blk, first, high, 0);
+    __syncthreads();
+    if (threadIdx.x == 0 && high > first) a.high_water[blk] = static_cast<int32_t>(first);
 }
 
 __global__ void __launch_bounds__(kPlanThreads) truncate_finish_kernel(TruncateArgs t) {
@@ -357,7 +384,8 @@ __global__ void __launch_bounds__(kPlanThreads) fork_kernel(Alloc a, const int32
 }
 
 sdc_status_t to_alloc(const sdc_page_allocator_t* in, Alloc* out) {
-    if (in == nullptr || in->free_bits == nullptr || in->refcount == nullptr || in->block_order == nullptr ||
+    if (in == nullptr || in->free_bits == nullptr || in->refcount == nullptr || in->high_water == nullptr ||
+        in->block_order == nullptr ||
         in->heap_of == nullptr || in->block_tables == nullptr || in->context_lens == nullptr) {
         return SDC_STATUS_NULL_ARGUMENT;
     }
@@ -369,8 +397,8 @@ sdc_status_t to_alloc(const sdc_page_allocator_t* in, Alloc* out) {
         in->block_size > (int64_t(1) << 31) / in->table_stride) {
         return SDC_STATUS_OVERFLOW;
     }
-    *out = Alloc{in->free_bits, in->refcount, in->block_order, in->heap_of, in->block_tables, in->context_lens,
-                 in->num_blocks, in->block_size, in->table_rows, in->table_stride};
+    *out = Alloc{in->free_bits, in->refcount, in->high_water, in->block_order, in->heap_of, in->block_tables,
+                 in->context_lens, in->num_blocks, in->block_size, in->table_rows, in->table_stride};
     return SDC_STATUS_OK;
 }
 

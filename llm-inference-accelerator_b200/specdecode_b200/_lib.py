@@ -179,6 +179,7 @@ class PageAllocator(ctypes.Structure):
     _fields_ = [
         ("free_bits", ctypes.c_void_p),
         ("refcount", ctypes.c_void_p),
+        ("high_water", ctypes.c_void_p),
         ("block_order", ctypes.c_void_p),
         ("heap_of", ctypes.c_void_p),
         ("block_tables", ctypes.c_void_p),

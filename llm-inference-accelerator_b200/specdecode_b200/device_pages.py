@@ -113,6 +113,7 @@ class DevicePagedCache:
         self.value_scale_pages = torch.zeros_like(self.key_scale_pages)
         self.free_bits = torch.from_numpy(words.view(np.int32)).to(dev)
         self.refcount = torch.zeros(nb, dtype=torch.int32, device=dev)
+        self.high_water = torch.zeros(nb, dtype=torch.int32, device=dev)
         self.block_order = torch.from_numpy(order.astype(np.int32)).to(dev)
         self.heap_of = torch.from_numpy(heap_of.astype(np.int32)).to(dev)
         self.block_tables = torch.full((max_rows, stride), -1, dtype=torch.int32, device=dev)
@@ -123,7 +124,8 @@ class DevicePagedCache:
             self.value_scale_pages.data_ptr(), nb, bs, L, H, D,
             L * H * bs * D, H * bs * D, bs * D, L * H * bs, H * bs, bs)
         self.allocator_desc = _lib.PageAllocator(
-            self.free_bits.data_ptr(), self.refcount.data_ptr(), self.block_order.data_ptr(),
+            self.free_bits.data_ptr(), self.refcount.data_ptr(), self.high_water.data_ptr(),
+            self.block_order.data_ptr(),
             self.heap_of.data_ptr(), self.block_tables.data_ptr(), self.context_lens.data_ptr(), nb, bs,
             max_rows, stride)
         self.length_bound = np.zeros(max_rows, dtype=np.int64)

@@ -124,11 +124,11 @@ def test_page_allocator_entry_points_validate_on_the_host(lib):
     assert h.sdc_pages_append_workspace_size(4, 100, 16, ctypes.byref(size)) == 0 and size.value > 0
     assert h.sdc_pages_append_workspace_size(0, 100, 16, ctypes.byref(size)) == _lib.STATUS_INVALID_SIZE
     assert h.sdc_pages_append_workspace_size(1025, 100, 16, ctypes.byref(size)) == _lib.STATUS_INVALID_SIZE
-    alloc = _lib.PageAllocator(None, 16, 16, 16, 16, 16, 64, 16, 4, 8)
+    alloc = _lib.PageAllocator(None, 16, 16, 16, 16, 16, 16, 64, 16, 4, 8)
     buf = ctypes.c_void_p(16)
     assert h.sdc_pages_append(ctypes.byref(alloc), None, buf, buf, 1, 1, buf, buf, 64, None, 0) == \
         _lib.STATUS_NULL_ARGUMENT
     assert h.sdc_pages_truncate(ctypes.byref(alloc), None, buf, buf, 1, 1, None, 0) == _lib.STATUS_NULL_ARGUMENT
     assert h.sdc_pages_fork(ctypes.byref(alloc), buf, buf, 1, None, 0) == _lib.STATUS_NULL_ARGUMENT
-    alloc = _lib.PageAllocator(16, 16, 16, 16, 16, 16, 0, 16, 4, 8)
+    alloc = _lib.PageAllocator(16, 16, 16, 16, 16, 16, 16, 0, 16, 4, 8)
     assert h.sdc_pages_fork(ctypes.byref(alloc), buf, buf, 1, None, 0) == _lib.STATUS_INVALID_SIZE
