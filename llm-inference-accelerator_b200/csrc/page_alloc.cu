@@ -25,7 +25,7 @@ namespace sdc {
 namespace {
 
 constexpr int kPlanThreads = 1024;
-constexpr int kCopyThreads = 256;
+constexpr int kCopyThreads = 128;
 
 struct Alloc {
     uint32_t* free_bits;
@@ -280,15 +280,17 @@ __device__ __forceinline__ bool truncate_valid(const TruncateArgs& t, int s, int
 //   1. truncate_mark_kernel (a thread per row): drops one reference from
 //      every block past the new length; a block whose last reference goes
 //      is marked -1 (released in this call) instead of 0;
-//   2. truncate_zero_kernel (a block per row and page): zeroes a released
-//      page's written rows, and the rows past the new length of the partly
-//      kept last page when this row alone holds it (a shared page's rows
-//      still belong to the other rows) -- up to the page's high-water mark,
-//      the rows any holder has written -- so freed pages and slots past a
-//      length hold zeros, as the reference's rollback leaves them;
-//   3. truncate_finish_kernel (a thread per row): returns the marked blocks
-//      to the free set (the first row to claim a block does it), clears the
-//      table entries and sets the length.
+//   2. truncate_zero_kernel (a block per touched page, row and layer):
+//      zeroes a released page's written rows, and the rows past the new
+//      length of the partly kept last page when this row alone holds it (a
+//      shared page's rows still belong to the other rows) -- up to the
+//      page's high-water mark, the rows any holder has written -- so freed
+//      pages and slots past a length hold zeros, as the reference's
+//      rollback leaves them;
+//   3. truncate_finish_kernel (a thread per row): lowers the high-water
+//      marks of the zeroed pages, returns the marked blocks to the free set
+//      (the first row to claim a block does it), clears the table entries
+//      and sets the length.
 __global__ void __launch_bounds__(kPlanThreads) truncate_mark_kernel(TruncateArgs t) {
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= t.sequences) return;
@@ -310,37 +312,52 @@ __global__ void __launch_bounds__(kPlanThreads) truncate_mark_kernel(TruncateArg
     }
 }
 
+// Block (touched page j, row s, layer) zeroes the rows to clear of that page
+// and layer -- every head, keys and values, codes and scales -- one 16-byte
+// chunk per thread.
 __global__ void __launch_bounds__(kCopyThreads) truncate_zero_kernel(TruncateArgs t) {
-    const int s = blockIdx.x;
+    const Alloc& a = t.a;
+    const Pool& pool = t.pool;
+    const int s = blockIdx.y;
+    const int64_t layer = blockIdx.z;
     int32_t row;
     int64_t old, now;
     if (!truncate_valid(t, s, &row, &old, &now) || now == old) return;
-    const Alloc& a = t.a;
-    const int64_t b = now / a.block_size + blockIdx.y;
-    if (b >= blocks_for(old, a.block_size)) return;
+    const int64_t bs = a.block_size;
+    const int64_t b = now / bs + blockIdx.x;
+    if (b >= blocks_for(old, bs)) return;
     const int32_t blk = a.tables[row * a.stride + b];
     if (blk < 0 || blk >= a.num_blocks) return;
-    __shared__ int32_t s_high;
-    int64_t first;
-    if (b < blocks_for(now, a.block_size)) {
-        // the partly kept last page: its rows past the new length, when this row alone holds it
-        if (a.refcount[blk] != 1) return;
-        first = now % a.block_size;
+    int first;
+    if (b < blocks_for(now, bs)) {
+        if (a.refcount[blk] != 1) return;  // a shared kept page's rows belong to its other holders
+        first = static_cast<int>(now % bs);
     } else if (a.refcount[blk] == -1) {
-        first = 0;  // released in this call: every written row
+        first = 0;  // released in this call
     } else {
         return;
     }
-    // rows at or past `first` that may hold data: up to the page's high water,
-    // read once so that every thread of the block zeroes the same rows (a
-    // page released by several rows has several blocks; whichever resets the
-    // mark has zeroed the rows first)
-    if (threadIdx.x == 0) s_high = a.high_water[blk];
-    __syncthreads();
-    const int64_t high = s_high;
-    page_rows(t.pool, -1, blk, first, high, 0);
-    __syncthreads();
-    if (threadIdx.x == 0 && high > first) a.high_water[blk] = static_cast<int32_t>(first);
+    const int rows = a.high_water[blk] - first;
+    if (rows <= 0) return;
+    const int H = static_cast<int>(pool.num_heads);
+    const int row_chunks = static_cast<int>(pool.head_dim / 16);
+    const int per_head = rows * row_chunks;
+    for (int c = threadIdx.x; c < 2 * H * per_head; c += blockDim.x) {
+        const int kvh = c / per_head, rem = c - kvh * per_head;
+        const int r = first + rem / row_chunks, ch = rem % row_chunks;
+        const bool value_side = kvh >= H;
+        const int head = value_side ? kvh - H : kvh;
+        int8_t* codes = (value_side ? pool.values : pool.keys) + blk * pool.cbs + layer * pool.cls +
+                        head * pool.chs + r * pool.head_dim + ch * 16;
+        *reinterpret_cast<uint4*>(codes) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    for (int i = threadIdx.x; i < 2 * H * rows; i += blockDim.x) {
+        const int kvh = i / rows, r = first + i % rows;
+        const bool value_side = kvh >= H;
+        const int head = value_side ? kvh - H : kvh;
+        float* scales = value_side ? pool.value_scales : pool.key_scales;
+        scales[blk * pool.sbs + layer * pool.sls + head * pool.shs + r] = 0.0f;
+    }
 }
 
 __global__ void __launch_bounds__(kPlanThreads) truncate_finish_kernel(TruncateArgs t) {
@@ -351,11 +368,19 @@ __global__ void __launch_bounds__(kPlanThreads) truncate_finish_kernel(TruncateA
     if (!truncate_valid(t, s, &row, &old, &now)) return;
     const Alloc& a = t.a;
     int32_t* table = a.tables + row * a.stride;
+    if (now < old && now % a.block_size != 0) {
+        // the kept page's rows past the new length were zeroed if this row alone holds it
+        const int32_t blk = table[now / a.block_size];
+        if (blk >= 0 && blk < a.num_blocks && a.refcount[blk] == 1) {
+            a.high_water[blk] = min(a.high_water[blk], static_cast<int32_t>(now % a.block_size));
+        }
+    }
     for (int64_t b = blocks_for(now, a.block_size); b < blocks_for(old, a.block_size); ++b) {
         const int32_t blk = table[b];
         table[b] = -1;
         if (blk < 0 || blk >= a.num_blocks) continue;
         if (atomicCAS(a.refcount + blk, -1, 0) == -1) {
+            a.high_water[blk] = 0;  // zeroed by the previous launch
             const int32_t h = a.heap_of[blk];
             atomicOr(a.free_bits + (h >> 5), 1u << (h & 31));
         }
@@ -489,7 +514,9 @@ SDC_API sdc_status_t sdc_pages_truncate(const sdc_page_allocator_t* allocator, c
         if (max_removed > 0) {
             // pages a truncation of at most max_removed tokens touches
             const int64_t pages = (max_removed + a.block_size - 1) / a.block_size + 1;
-            truncate_zero_kernel<<<dim3(static_cast<unsigned>(sequences), static_cast<unsigned>(pages)),
+            if (pool->num_layers > 65535) return SDC_STATUS_UNSUPPORTED;
+            truncate_zero_kernel<<<dim3(static_cast<unsigned>(pages), static_cast<unsigned>(sequences),
+                                        static_cast<unsigned>(pool->num_layers)),
                                    kCopyThreads, 0, s>>>(t);
         }
         truncate_finish_kernel<<<row_blocks, kPlanThreads, 0, s>>>(t);
