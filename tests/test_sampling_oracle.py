@@ -171,3 +171,14 @@ def test_oracle_matches_the_reference_library_on_generated_rows(reference_librar
         both(lambda m: m.acceptance_probabilities([t], [d], [token]))
 
     check()
+
+
+@pytest.mark.parametrize("record", GOLDEN["cases"], ids=lambda r: r["name"])
+def test_round_decisions_do_not_depend_on_normalising_first(record):
+    """The device round takes the rows as stored (softmax output, not
+    renormalised the way the decoder's ``_probabilities`` does); on every
+    case the reference functions reach the same decisions either way."""
+    case = CASES[record["name"]]
+    got = orc.verify_round(rows(case.target), rows(case.draft), case.proposed, case.uniforms, case.bonus)
+    want = record["round"]
+    assert (got.accepted, got.token, got.draws) == (want["accepted"], want["token"], want["draws"])
