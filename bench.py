@@ -49,6 +49,13 @@ SPEC = dict(batch=64, prompt=1024, new_tokens=64, window=5, min_window=4, max_wi
             vocab=128256,
             draft=dict(layers=16, hidden=2048, heads=32, kv_heads=8, head_dim=64, intermediate=8192),
             target=dict(layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128, intermediate=14336))
+# the CPU-runnable workload of the reference: 4 sequences prefill 512 fp32
+# tokens, then 64 rounds append a 5-token window each and keep the prefix
+# accepted by Bernoulli(0.7) draws up to the first rejection
+CONFIG1 = dict(layers=16, kv_heads=8, head_dim=64, block_size=16, num_blocks=4096, sequences=4, prefill=512,
+               rounds=64, window=5, accept_p=0.7)
+VERIFY_WORKLOAD = ("8B verify attention: B32 Hq32 Hkv8 D128 window5 ctx U[1024,8192] bs16, "
+                   "randomly permuted physical blocks, one layer")
 FLUSH_BYTES = 256 << 20
 HOLD_CYCLES = 200_000  # about 0.1 ms of device time at B200 clocks
 
@@ -72,6 +79,8 @@ def parse_args(argv=None):
     p.add_argument("--seed", type=int, default=2024)
     p.add_argument("--skip-append", action="store_true", help="measure only the verify attention")
     p.add_argument("--skip-cpu-baseline", action="store_true")
+    p.add_argument("--skip-config1", action="store_true",
+                   help="skip the CPU-runnable workload (16 layers, 4 sequences, 64 speculative rounds) on the GPU")
     p.add_argument("--skip-long", action="store_true", help="skip the 70B long-context (KV-head parallel) workload")
     p.add_argument("--skip-speculative", action="store_true",
                    help="skip the end-to-end speculative decoding workload (draft 16L d2048 / target 32L d4096)")
@@ -223,32 +232,41 @@ def sum_over_ranks(value: float, world: int) -> float:
 # verify attention (headline)
 # ---------------------------------------------------------------------------
 
-def verify_inputs(seed: int):
+def verify_inputs(seed: int, rank: int = 0, world: int = 1):
+    """Context lengths, a block table over a permuted pool, bf16-valued
+    queries and the pool's block count for this rank's share of one global
+    batch of ``32 * world`` sequences drawn from ``seed``, split over the
+    ranks longest-first (balanced total context)."""
     import numpy as np
 
     rng = np.random.default_rng(seed)
     v = VERIFY
-    lens = rng.integers(v["min_context"], v["max_context"] + 1, size=v["batch"])
+    lens = rng.integers(v["min_context"], v["max_context"] + 1, size=v["batch"] * world)
+    if world > 1:
+        from specdecode_b200.sharding import lpt_partition
+
+        lens = lens[lpt_partition(lens.tolist(), world)[rank]]
+        rng = np.random.default_rng([seed, rank])
     blocks = (lens + v["block_size"] - 1) // v["block_size"]
     nb = int(blocks.sum())
     perm = rng.permutation(nb)
-    table = np.full((v["batch"], int(blocks.max())), -1, dtype=np.int32)
+    table = np.full((len(lens), int(blocks.max())), -1, dtype=np.int32)
     at = 0
     for b, n in enumerate(blocks):
         table[b, :n] = perm[at:at + n]
         at += n
-    query = rng.standard_normal((v["batch"], v["query_heads"], v["window"], v["head_dim"]), dtype=np.float32)
+    query = rng.standard_normal((len(lens), v["query_heads"], v["window"], v["head_dim"]), dtype=np.float32)
     return lens.astype(np.int64), table, nb, query
 
 
-def build_verify(seed: int, device):
+def build_verify(seed: int, device, rank: int = 0, world: int = 1):
     import torch
 
     from specdecode_b200.cuda_kv_cache import PagedVerifyAttention, attention_bytes
     from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
 
     v = VERIFY
-    lens, table, nb, query = verify_inputs(seed)
+    lens, table, nb, query = verify_inputs(seed, rank, world)
     cache = PagedKVCache(KVCacheConfig(1, v["kv_heads"], v["head_dim"], block_size=v["block_size"], num_blocks=nb),
                          device=device, max_sequences=1, check_status=False)
     gen = torch.Generator(device=device).manual_seed(seed)
@@ -838,63 +856,228 @@ def run_long_context(seed: int, rank: int, world: int, device, steps: int, warmu
     }
 
 
-def cpu_attention_baseline(state, budget_s: float = 12.0):
-    """The reference's unfused op (dequantize in bf16, expand GQA heads,
-    boolean mask, SDPA) restated with CPU torch, over as many of the
-    benchmark's sequences as fit in ``budget_s``."""
+def verify_seq_bytes(lens):
+    """Algorithmic bytes of each sequence's share of a verify-attention call:
+    its cached tokens' INT8 key / value codes and fp32 scales for every KV
+    head, its bf16 query and output rows and its block-table entries (their
+    sum over a batch is ``attention_bytes``)."""
+    v = VERIFY
+    per_token = 2 * v["kv_heads"] * v["head_dim"] + 2 * v["kv_heads"] * 4
+    rows = v["query_heads"] * v["window"] * v["head_dim"] * 2
+    return [int(T) * per_token + 2 * rows + -(-int(T) // v["block_size"]) * 4 for T in lens]
+
+
+def config1_events(seed: int, only=None):
+    """The reference's CPU-runnable workload: ``("append", seq, keys,
+    values)`` with float32 N(0,1) ``[tokens, 16, 8, 64]`` arrays and
+    ``("truncate", seq, new_length)``.  Every sequence prefills 512 tokens;
+    then each of 64 rounds appends a 5-token window to every sequence and
+    keeps the prefix accepted by Bernoulli(0.7) draws up to the first
+    rejection.  ``only``: yield just that sequence's events (the draws are
+    the same as for the whole workload)."""
+
+    for event in _config1_all(seed):
+        if only is None or event[1] == only:
+            yield event
+
+
+def _config1_all(seed: int):
+    import numpy as np
+
+    c = CONFIG1
+    rng = np.random.default_rng(seed)
+    dims = (c["layers"], c["kv_heads"], c["head_dim"])
+    lengths = [0] * c["sequences"]
+    for s in range(c["sequences"]):
+        yield ("append", s, rng.standard_normal((c["prefill"], *dims), dtype=np.float32),
+               rng.standard_normal((c["prefill"], *dims), dtype=np.float32))
+        lengths[s] = c["prefill"]
+    for _ in range(c["rounds"]):
+        for s in range(c["sequences"]):
+            yield ("append", s, rng.standard_normal((c["window"], *dims), dtype=np.float32),
+                   rng.standard_normal((c["window"], *dims), dtype=np.float32))
+            accepted = 0
+            while accepted < c["window"] and rng.random() < c["accept_p"]:
+                accepted += 1
+            lengths[s] += accepted
+            yield ("truncate", s, lengths[s])
+
+
+def append_events(seed: int, sequences: int, steps: int):
+    """The append workload's speculative step for ``sequences`` of its
+    sequences: each step appends a 5-token window of bf16-valued N(0,1) keys
+    and values (32 layers x 8 heads x 128, scaled by per-head factors
+    log-uniform in [0.1, 10]) to every sequence, then rolls 0-5 tokens back."""
+    import numpy as np
     import torch
 
-    from oracle.attention import attention_reference_torch_flat
-    from specdecode_b200.cuda_kv_cache import attention_bytes
+    a = APPEND
+    rng = np.random.default_rng(seed)
+    factors = np.exp(rng.uniform(math.log(0.1), math.log(10.0), size=(1, 1, a["kv_heads"], 1)))
+    dims = (a["window"], a["layers"], a["kv_heads"], a["head_dim"])
 
-    torch.set_num_threads(os.cpu_count() or 1)
-    cache = state["cache"]
+    def draw():
+        x = (rng.standard_normal(dims) * factors).astype(np.float32)
+        return torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+
+    lengths = [0] * sequences
+    for _ in range(steps):
+        for s in range(sequences):
+            yield ("append", s, draw(), draw())
+            lengths[s] += a["window"]
+        for s in range(sequences):
+            lengths[s] -= int(rng.integers(0, a["window"] + 1))
+            yield ("truncate", s, lengths[s])
+
+
+def cpu_reference_attention(lens, table, query, pool, *, budget_s: float, min_passes: int = 1):
+    """The reference's own paged attention on the host cores (CPU baseline
+    leg (i)): ``submit_paged_attention`` unchanged, one call per sequence."""
+    from oracle import reference_runs as rr
+
+    order, seconds, _ = rr.time_submit_paged_attention(pool, lens, table, query, VERIFY["block_size"], budget_s,
+                                                       min_passes=min_passes)
+    per = verify_seq_bytes(lens)
+    t = sum(seconds)
+    passes = len(order) / len(lens)
+    return {"value": sum(per[b] for b in order) / t / 1e9, "unit": "GB/s", "cores": rr.host_threads(),
+            "kind": "reference",
+            "sample": f"the reference's submit_paged_attention (src/specdecode/cuda_kv_cache.py:370-503, unchanged, "
+                      f"imported from oracle/_ref) on CPU torch through an inline runtime shim, one call per "
+                      f"sequence (its API is batch 1): {len(order)} calls = {passes:.2f} passes over the "
+                      f"{len(lens)} sequences ({sum(int(lens[b]) for b in order)} cached tokens), {t:.1f} s",
+            "ms_per_pass": 1e3 * t / passes}
+
+
+def cpu_reference_reconstruct(lens, query, *, budget_s: float, seed: int):
+    """CPU baseline leg (ii): the reference's CPU reconstruct path, the
+    native dequantization plus Python reconstruction of
+    ``materialize_legacy_cache`` and torch CPU SDPA."""
+    from oracle import reference_runs as rr
+
     v = VERIFY
-    keys = cache.keys_view[:, :, 0].cpu()
-    vals = cache.values_view[:, :, 0].cpu()
-    ks = cache.key_scales_view[:, :, 0].cpu()
-    vs = cache.value_scales_view[:, :, 0].cpu()
-    q = torch.from_numpy(state["query"]).to(torch.bfloat16)
-    done, elapsed, lens_done = 0, 0.0, []
-    for b in range(v["batch"]):
-        T = int(state["lens"][b])
-        t = torch.arange(T)
-        blk = torch.from_numpy(state["table"][b]).long()[t // v["block_size"]]
-        off = t % v["block_size"]
+    r = rr.time_reconstruct_attention(lens, query, v["kv_heads"], v["head_dim"], v["block_size"], budget_s, seed)
+    n = r["sequences"]
+    return {"value": sum(verify_seq_bytes(lens[:n])) / r["seconds"] / 1e9, "unit": "GB/s", "cores": r["threads"],
+            "kind": "reference",
+            "sample": f"the reference's HuggingFacePagedCacheMirror.materialize_legacy_cache "
+                      f"(src/specdecode/hf_paged_cache.py:247-313: NativeKVQuantizer dequantization over the "
+                      f"reference's library, Python reconstruction) + GQA expansion + torch CPU SDPA in bf16, "
+                      f"first {n} of {len(lens)} sequences ({r['tokens']} cached tokens), {r['seconds']:.1f} s",
+            "synchronize_tokens_per_s": r["tokens"] / r["synchronize_seconds"]}
+
+
+def cpu_reference_append(events, shape: dict, *, budget_s: float, what: str):
+    """The reference's ``PagedKVCache.append_many`` / ``truncate`` with its
+    ``NativeKVQuantizer`` over ``events`` until ``budget_s`` of timed work."""
+    from oracle import reference_runs as rr
+
+    r = rr.time_append_rollback(shape["layers"], shape["kv_heads"], shape["head_dim"], shape["block_size"],
+                                shape["num_blocks"], events, budget_s)
+    return {"value": r["appended_tokens"] / r["append_seconds"], "unit": "tokens/s", "cores": 1,
+            "kind": "reference",
+            "rollback_tokens_per_s": r["rolled_back_tokens"] / r["truncate_seconds"] if r["truncate_seconds"] else None,
+            "sample": f"the reference's PagedKVCache.append_many + truncate (src/specdecode/kv_cache.py:290-336, "
+                      f":395-420) with NativeKVQuantizer over the reference's library, one Python thread: {what}, "
+                      f"{r['events']} calls over {r['sequences']} sequences, {r['appended_tokens']} tokens appended "
+                      f"in {r['append_seconds']:.1f} s, {r['rolled_back_tokens']} rolled back in "
+                      f"{r['truncate_seconds']:.2f} s"}
+
+
+def run_config1(seed: int, device, repeats: int = 3):
+    """The reference's CPU-runnable workload through this library's
+    ``PagedKVCache`` on the GPU: every append copies its float32 keys and
+    values from pinned host memory, every rollback is kernel (b).  Wall time
+    of the whole workload through the Python API, best of ``repeats`` runs
+    after one warm-up run, each on a fresh cache."""
+    import torch
+
+    from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
+
+    c = CONFIG1
+    events = []
+    appended = rolled = h2d = 0
+    lengths = [0] * c["sequences"]
+    for e in config1_events(seed):
+        if e[0] == "append":
+            k, v = torch.from_numpy(e[2]).pin_memory(), torch.from_numpy(e[3]).pin_memory()
+            events.append(("append", e[1], k, v))
+            appended += k.shape[0]
+            lengths[e[1]] += k.shape[0]
+            h2d += 2 * k.numel() * k.element_size()
+        else:
+            rolled += lengths[e[1]] - e[2]
+            lengths[e[1]] = e[2]
+            events.append(e)
+
+    def once():
+        cache = PagedKVCache(KVCacheConfig(c["layers"], c["kv_heads"], c["head_dim"], block_size=c["block_size"],
+                                           num_blocks=c["num_blocks"]), device=device, check_status=False)
+        for s in range(c["sequences"]):
+            cache.create_sequence(s)
+        torch.cuda.synchronize()
         t0 = time.perf_counter()
-        attention_reference_torch_flat(q[b], keys[blk, off], vals[blk, off], ks[blk, off], vs[blk, off])
-        elapsed += time.perf_counter() - t0
-        done += 1
-        lens_done.append(T)
-        if elapsed > budget_s:
-            break
-    nbytes = attention_bytes(lens_done, v["query_heads"], v["kv_heads"], v["head_dim"], v["window"], v["block_size"])
-    return {"value": nbytes / elapsed / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{done} of {v['batch']} sequences ({sum(lens_done)} cached tokens), unfused "
-                      f"dequantize-then-SDPA in bf16 on CPU torch, {elapsed:.1f} s"}
+        for e in events:
+            if e[0] == "append":
+                cache.append_tensor(e[1], e[2], e[3])
+            else:
+                cache.truncate(e[1], e[2])
+        torch.cuda.synchronize()
+        t = time.perf_counter() - t0
+        if cache.status_bits():
+            raise RuntimeError("device fault in the CPU-runnable workload")
+        return t
+
+    once()
+    t = min(once() for _ in range(repeats))
+    return {"workload": "L16 Hkv8 D64 bs16, 4096 blocks, fp32 N(0,1) keys/values from pinned host memory: 4 sequences "
+                        "prefill 512 tokens, 64 rounds append a 5-token window each and roll back past the first "
+                        "Bernoulli(0.7) rejection",
+            "appended_tokens": appended, "rolled_back_tokens": rolled, "seconds": t,
+            "tokens_per_s": appended / t, "h2d_bytes": h2d}
 
 
 def run_reference_arm(args, rank: int, world: int) -> None:
+    """The reference's own CPU path on this host's cores, never this
+    library: the config-2 pool is quantized by the oracle's C restatement of
+    the reference rule and the timed calls are the reference's code from
+    oracle/_ref.  Rank 0 alone runs; other ranks return at once."""
     if rank != 0:
         return
-    import torch
+    from oracle import reference_runs as rr
 
-    from specdecode_b200.kv_cache import KVCacheConfig  # noqa: F401  (package import check)
-
-    device = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    if device is None:
-        print(json.dumps({"impl": "reference", "unavailable": "no CUDA device to build the benchmark pool"}))
+    try:
+        rr.reference_package()
+    except rr.ReferenceUnavailable as error:
+        print(json.dumps({"impl": "reference", "unavailable": str(error)}))
         return
-    state = build_verify(args.seed, device)
-    budget = max(3.0, min(25.0, 0.5 * args.steps))
-    base = cpu_attention_baseline(state, budget_s=budget)
+    v = VERIFY
+    lens, table, nb, query = verify_inputs(args.seed)
+    pool = rr.verify_pool(nb, v["kv_heads"], v["head_dim"], v["block_size"], args.seed)
+    # warm-up passes, then K timed passes (one step = one pass over the batch),
+    # fewer if a pass is slow enough that K would exceed about a minute
+    warm = cpu_reference_attention(lens, table, query, pool, budget_s=0.0, min_passes=1)
+    for _ in range(min(args.warmup, 3) - 1):
+        cpu_reference_attention(lens, table, query, pool, budget_s=0.0, min_passes=1)
+    passes = max(1, min(args.steps, int(60.0 / max(warm["ms_per_pass"] / 1e3, 1e-3))))
+    base = cpu_reference_attention(lens, table, query, pool, budget_s=0.0, min_passes=passes)
+    reconstruct = cpu_reference_reconstruct(lens, query, budget_s=6.0, seed=args.seed + 7)
+    append = cpu_reference_append(append_events(args.seed + 1, 4, 1000), APPEND, budget_s=8.0,
+                                  what="the append workload's step for 4 of its 256 sequences")
+    config1 = cpu_reference_append(config1_events(args.seed, only=0), CONFIG1, budget_s=10.0,
+                                   what="sequence 0 of the CPU-runnable workload's 4 (prefill, then its rounds)")
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V quantized to INT8 pages)",
-        "config": {"workload": "8B verify attention: B32 Hq32 Hkv8 D128 window5 ctx U[1024,8192] bs16"},
+        "steps": args.steps, "warmup": args.warmup, "passes_timed": passes, "ms_per_step": base["ms_per_pass"],
+        "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 K/V quantized to INT8 pages, N(0,1) bf16 queries)",
+        "config": {"workload": VERIFY_WORKLOAD},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reconstruct_path": reconstruct,
+        "append": append,
+        "config1": config1,
     }
     print(json.dumps(line))
 
@@ -922,7 +1105,7 @@ def main(argv=None) -> int:
         run_sampling(args.seed, device, args.steps, args.warmup, profile_only=True)
         return 0
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
-    state = build_verify(args.seed + 1000 * rank, device)
+    state = build_verify(args.seed, device, rank, world)
 
     if args.profile:
         t_ms, _, _, _ = time_verify(state, args.steps, args.warmup, world, flush)
@@ -978,9 +1161,29 @@ def main(argv=None) -> int:
     if not args.skip_speculative:
         speculative = run_speculative(args.seed + 1000 * rank, device, world)
 
-    cpu = None
+    cpu = config1 = None
+    if not args.skip_config1:
+        config1 = run_config1(args.seed + 1000 * rank, device)
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
-        cpu = cpu_attention_baseline(state)
+        # the reference's own CPU path on this host, bounded samples of the
+        # same workloads (the attention leg reads this run's pool)
+        cache = state["cache"]
+        pool = {"keys": cache.keys_view[:, :, :1].contiguous().cpu().numpy(),
+                "values": cache.values_view[:, :, :1].contiguous().cpu().numpy(),
+                "key_scales": cache.key_scales_view[:, :, :1].contiguous().cpu().numpy(),
+                "value_scales": cache.value_scales_view[:, :, :1].contiguous().cpu().numpy()}
+        cpu = cpu_reference_attention(state["lens"], state["table"], state["query"], pool, budget_s=3.0)
+        del pool
+        cpu["reconstruct_path"] = cpu_reference_reconstruct(state["lens"], state["query"], budget_s=4.0,
+                                                            seed=args.seed + 7)
+        if append is not None:
+            append["cpu_baseline"] = cpu_reference_append(
+                append_events(args.seed + 1, 4, 1000), APPEND, budget_s=6.0,
+                what="the append workload's step for 4 of its 256 sequences")
+        if config1 is not None:
+            config1["cpu_baseline"] = cpu_reference_append(
+                config1_events(args.seed, only=0), CONFIG1, budget_s=8.0,
+                what="sequence 0 of the CPU-runnable workload's 4 (prefill, then its rounds)")
 
     clocks = sampler.summary(w0 - 1.2, w1 + 0.1) if sampler is not None else None
     if rank == 0:
@@ -998,10 +1201,10 @@ def main(argv=None) -> int:
             "dtype": "int8 pages, fp32 softmax/accumulate",
             "data": "synthetic (seeded N(0,1) bf16 K/V quantized to INT8 pages, N(0,1) bf16 queries)",
             "config": {
-                "workload": "8B verify attention: B32 Hq32 Hkv8 D128 window5 ctx U[1024,8192] bs16, "
-                            "randomly permuted physical blocks, one layer",
-                "per_gpu_batch": VERIFY["batch"],
-                "parallelism": f"request data-parallel x{world} (no collective)",
+                "workload": VERIFY_WORKLOAD,
+                "global_batch": VERIFY["batch"] * world,
+                "parallelism": f"request data-parallel x{world} (no collective): one batch of "
+                               f"{VERIFY['batch'] * world} sequences split over the ranks longest-first",
                 "l2": "256 MiB flush between timed iterations; pool larger than L2",
             },
             "fraction_of_peak": value / world / peak,
@@ -1012,6 +1215,7 @@ def main(argv=None) -> int:
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": 3 * args.steps,
             "append": append,
+            "config1": config1,
             "long_context_70b": long_ctx,
             "device_pages": device_pages,
             "speculative_sampling": sampling,

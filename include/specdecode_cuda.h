@@ -228,7 +228,9 @@ SDC_API sdc_status_t sdc_paged_verify_attention(
  * before any launch.  Calls on one device share the array: calls that overlap
  * on the GPU race, so keep them on one stream.  The first call on a device
  * looks up the array's address with that device current; make it before any
- * stream capture.  No counterpart in the reference.
+ * stream capture.  That address is cached for the life of the process: do not
+ * call this entry point on a device again after cudaDeviceReset.  No
+ * counterpart in the reference.
  */
 SDC_API sdc_status_t sdc_paged_verify_attention_no_alloc(
     const sdc_page_pool_t* pool, int64_t layer, const void* query, int query_dtype,

@@ -23,7 +23,10 @@
 // streams, or from different threads) race on it; order such calls on one
 // stream.  The first call on each device looks up the array's device
 // address (cudaGetSymbolAddress, with that device current) and caches it;
-// make that first call before any stream capture.
+// make that first call before any stream capture.  The cached address is
+// never refreshed, so after cudaDeviceReset (or anything else that destroys
+// and recreates the device's primary context) this entry point must not be
+// called again on that device in the same process.
 
 #include <mutex>
 

@@ -17,6 +17,14 @@ Keeps the reference's device-side surface (src/specdecode/cuda_kv_cache.py):
   gather/dequantize/GQA/mask/SDPA sequence is one fused kernel launch.
 
 ``PagedVerifyAttention`` is the batched form: many sequences, one launch.
+
+The ``runtime`` these functions take is the caller's own execution runtime,
+used as the reference's code uses its ``CudaExecutionRuntime``
+(src/specdecode/cuda.py): an object with a ``device`` attribute and
+``submit_target(fn, *, wait_for=(), label=...)`` /
+``submit_transfer(fn, *, wait_for=(), label=...)`` methods that run ``fn``
+on the runtime's target / transfer stream and return a task.  The
+reference's runtime works unchanged; this module defines none of its own.
 """
 
 from __future__ import annotations
@@ -27,7 +35,6 @@ from dataclasses import dataclass
 from typing import Any
 
 from . import _lib
-from .cuda import CudaExecutionRuntime, CudaTask
 from .kv_cache import KVCacheConfig, PagedKVCache, _dtype_code
 
 
@@ -159,7 +166,7 @@ def paged_verify_attention(cache: PagedKVCache, query, sequence_ids: Sequence[Ha
 class CudaPagedKVCacheStorage:
     """Binds one sequence of a device ``PagedKVCache`` for kernel consumption."""
 
-    def __init__(self, config: KVCacheConfig, runtime: CudaExecutionRuntime, *, name: str = "paged_kv") -> None:
+    def __init__(self, config: KVCacheConfig, runtime: Any, *, name: str = "paged_kv") -> None:
         if not isinstance(name, str) or not name.strip():
             raise ValueError("CUDA paged-cache storage name cannot be empty")
         self.config = config
@@ -203,7 +210,7 @@ class CudaPagedKVCacheStorage:
             raise CudaPagedKVCacheError("storage has not been synchronized")
         return self._view_of(self._cache, self._sequence_id, self._tokens)
 
-    def synchronize(self, cache: PagedKVCache, sequence_id: Hashable) -> CudaTask[CudaPagedKVCacheView]:
+    def synchronize(self, cache: PagedKVCache, sequence_id: Hashable) -> Any:
         self._validate(cache)
         length = cache.sequence_length(sequence_id)
         if self._sequence_id is not None and sequence_id != self._sequence_id:
@@ -225,8 +232,8 @@ class CudaPagedKVCacheStorage:
         return self.runtime.submit_transfer(lambda: view, label=f"specdecode.transfer.{self.name}.synchronize")
 
 
-def submit_paged_attention(runtime: CudaExecutionRuntime, query: Any, cache: CudaPagedKVCacheView,
-                           layer_index: int, *, wait_for: Sequence[CudaTask[Any]] = ()) -> CudaTask[Any]:
+def submit_paged_attention(runtime: Any, query: Any, cache: CudaPagedKVCacheView, layer_index: int, *,
+                           wait_for: Sequence[Any] = ()) -> Any:
     """Fused causal attention over one cached sequence (reference signature).
 
     ``query`` is ``[1, query_heads, query_tokens, head_dim]`` and stands for

@@ -10,8 +10,11 @@ reference's sampling functions and decoder.
   proposal counts, without bonus, on float32 and on unnormalised rows;
 * the reference tests' known answers and error cases through
   DeviceSamplingBackend (tests/test_native.py:40-90 of the reference);
-* whole decodes: SpeculativeDecoder with the device verification gives the
-  reference decoder's tokens, events, statistics and generator state;
+* whole decodes: the reference's own SpeculativeDecoder (src/specdecode/
+  decoder.py, unchanged, from the copy of its package in oracle/_ref/) with
+  DeviceSamplingBackend as its sampling backend gives the recorded tokens,
+  events, statistics and generator state, also when the target model scores
+  a whole proposal in one call (score_proposal);
 * a 64-sequence, 128 256-token-vocabulary round checked by properties that
   hold at any size.
 """
@@ -220,36 +223,22 @@ def test_faulted_sequences_are_marked_and_others_decided(device):
     assert (int(acc[0]), int(token[0])) == (want["accepted"], want["token"])
 
 
-class _Table:
-    def __init__(self, table, default):
-        self._table = {tuple(k): tuple(v) for k, v in table.items()}
-        self._default = tuple(default)
-        self.vocab_size = len(self._default)
+def _reference_decoder():
+    """The reference's decoder, config and table model from oracle/_ref/."""
+    from oracle.reference_runs import ReferenceUnavailable, reference_package
 
-    def next_token_probs(self, context):
-        context = tuple(context)
-        if context in self._table:
-            return self._table[context]
-        if context and (context[-1],) in self._table:
-            return self._table[(context[-1],)]
-        return self._default
+    try:
+        reference_package()
+    except ReferenceUnavailable as error:
+        pytest.skip(str(error))
+    from specdecode.config import DecodeConfig
+    from specdecode.decoder import SpeculativeDecoder
+    from specdecode.models import TableModel
+
+    return DecodeConfig, SpeculativeDecoder, TableModel
 
 
-@pytest.mark.parametrize("record", GOLDEN["decodes"], ids=lambda r: r["name"])
-def test_decoder_matches_the_reference_decoder(device, record):
-    """tests/test_native.py:92-124 of the reference, against its recorded run:
-    same tokens, events, statistics and generator state."""
-    from specdecode_b200.decoder import DecodeConfig, SpeculativeDecoder
-
-    run = next(r for r in sc.decode_runs() if r["name"] == record["name"])
-    (dt, dd), (tt, td) = sc.tables_for(run)
-    config = DecodeConfig(max_new_tokens=run["max_new_tokens"], eos_token_id=run["eos_token_id"],
-                          initial_draft_tokens=run.get("initial_draft_tokens", 4),
-                          dynamic_draft=run.get("dynamic_draft", True))
-    rng = random.Random(run["seed"])
-    events = []
-    result = SpeculativeDecoder(_Table(dt, dd), _Table(tt, td), config, rng=rng, device=device).generate(
-        run["prompt"], on_token=events.append)
+def _check_decode(result, events, rng, record):
     assert list(result.generated_tokens) == record["generated"]
     assert [e.source for e in events] == record["sources"]
     assert [e.index for e in events] == record["indices"]
@@ -258,6 +247,42 @@ def test_decoder_matches_the_reference_decoder(device, record):
                 rejected_tokens=s.rejected_tokens, target_tokens=s.target_tokens,
                 verification_rounds=s.verification_rounds, fallback_steps=s.fallback_steps) == record["stats"]
     assert hashlib.sha256(repr(rng.getstate()).encode()).hexdigest() == record["rng_sha"]
+
+
+@pytest.mark.parametrize("scoring", [False, True], ids=["next_token_probs", "score_proposal"])
+@pytest.mark.parametrize("record", GOLDEN["decodes"], ids=lambda r: r["name"])
+def test_reference_decoder_on_the_device_backend(device, record, scoring):
+    """The reference's SpeculativeDecoder, unchanged, drives the device
+    kernels through DeviceSamplingBackend and reproduces its recorded run
+    (made with its own native and Python backends, tests/test_native.py:92-124
+    of the reference).  With ``score_proposal`` the target's rows for a whole
+    proposal come from one call (src/specdecode/decoder.py:113-136), the path
+    the reference's Hugging Face adapter takes."""
+    from specdecode_b200.sampling import DeviceSamplingBackend
+
+    DecodeConfig, SpeculativeDecoder, TableModel = _reference_decoder()
+
+    class ScoringTable(TableModel):
+        calls = 0
+
+        def score_proposal(self, prefix, proposed):
+            ScoringTable.calls += 1
+            return [self.next_token_probs(list(prefix) + list(proposed[:i])) for i in range(len(proposed) + 1)]
+
+    run = next(r for r in sc.decode_runs() if r["name"] == record["name"])
+    (dt, dd), (tt, td) = sc.tables_for(run)
+    config = DecodeConfig(max_new_tokens=run["max_new_tokens"], eos_token_id=run["eos_token_id"],
+                          initial_draft_tokens=run.get("initial_draft_tokens", 4),
+                          dynamic_draft=run.get("dynamic_draft", True))
+    target = (ScoringTable if scoring else TableModel)(tt, td)
+    rng = random.Random(run["seed"])
+    events = []
+    decoder = SpeculativeDecoder(TableModel(dt, dd), target, config, rng=rng,
+                                 sampling_backend=DeviceSamplingBackend(device))
+    result = decoder.generate(run["prompt"], on_token=events.append)
+    _check_decode(result, events, rng, record)
+    if scoring:
+        assert ScoringTable.calls == result.stats.verification_rounds > 0
 
 
 def test_large_vocabulary_round_properties(device):

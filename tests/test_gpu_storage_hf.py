@@ -20,7 +20,16 @@ D = 16
 
 @pytest.fixture()
 def runtime(device):
-    from specdecode_b200.cuda import CudaExecutionRuntime, CudaRuntimeConfig
+    """The reference's own CudaExecutionRuntime (src/specdecode/cuda.py),
+    unchanged, from the copy of its package in oracle/_ref/: the storage
+    and attention entry points take the caller's runtime as it is."""
+    from oracle.reference_runs import ReferenceUnavailable, reference_package
+
+    try:
+        reference_package()
+    except ReferenceUnavailable as error:
+        pytest.skip(str(error))
+    from specdecode.cuda import CudaExecutionRuntime, CudaRuntimeConfig
 
     return CudaExecutionRuntime(CudaRuntimeConfig(device=f"cuda:{device.index}"))
 

@@ -1,41 +1,19 @@
-"""Host-side logic of the device sampling path, on the CPU: the decoder's
-configuration and row normalisation (src/specdecode/config.py:7-30,
-src/specdecode/sampling.py:14-36), its adaptive window
-(src/specdecode/decoder.py:47-60), and the mapping of device fault bits to
-the reference's status codes and messages (native/src/native.cpp:52-80)."""
+"""Host-side logic of the device sampling path, on the CPU: the batched
+driver's adaptive window (the reference's rule, src/specdecode/decoder.py:47-60)
+and the mapping of device fault bits to the reference's status codes and
+messages (native/src/native.cpp:52-80)."""
 
 from __future__ import annotations
-
-import math
 
 import pytest
 
 from specdecode_b200 import _lib
-from specdecode_b200.decoder import DecodeConfig, DistributionError, _Window, normalize_probabilities
 from specdecode_b200.sampling import raise_for_status
-
-
-def test_decode_config_validation():
-    DecodeConfig()
-    for kwargs in (dict(max_new_tokens=-1), dict(min_draft_tokens=0), dict(min_draft_tokens=3, max_draft_tokens=2),
-                   dict(initial_draft_tokens=9)):
-        with pytest.raises(ValueError):
-            DecodeConfig(**kwargs)
-
-
-def test_normalize_probabilities_follows_the_reference():
-    assert normalize_probabilities([2, 3]) == (0.4, 0.6)
-    row = normalize_probabilities([0.1] * 10)
-    assert math.fsum(row) == pytest.approx(1.0, abs=1e-15)
-    for bad in ([], [0, 0], [0.5, -0.5], [float("nan"), 1.0], [float("inf"), 1.0]):
-        with pytest.raises(DistributionError):
-            normalize_probabilities(bad)
-    with pytest.raises(DistributionError):
-        normalize_probabilities([1.0, 2.0], expected_size=3)
+from specdecode_b200.speculative import DraftWindow
 
 
 def test_window_follows_the_reference_rule():
-    w = _Window(DecodeConfig(initial_draft_tokens=4, min_draft_tokens=1, max_draft_tokens=8))
+    w = DraftWindow(size=4, min_size=1, max_size=8)
     w.observe(4, 4)
     assert w.size == 5  # full acceptance grows by one
     w.observe(2, 5)
@@ -44,7 +22,7 @@ def test_window_follows_the_reference_rule():
     assert w.size == 1  # otherwise shrinks by one, floored at the minimum
     w.observe(0, 0)
     assert w.size == 1  # no proposals: unchanged
-    fixed = _Window(DecodeConfig(dynamic_draft=False))
+    fixed = DraftWindow(size=4, dynamic=False)
     fixed.observe(4, 4)
     assert fixed.size == 4
 
