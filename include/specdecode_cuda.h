@@ -239,6 +239,19 @@ SDC_API sdc_status_t sdc_paged_verify_attention_no_alloc(
     int32_t* device_status, uintptr_t stream);
 
 /*
+ * Test hook of kernel (c)'s bounded pipeline waits, for the launches that
+ * follow in this process: every wait of the tensor-core item kernel gives up
+ * after wait_limit_cycles SM cycles (<= 0: the default, about one second),
+ * records SDC_FAULT_WAIT_TIMEOUT in device_status and winds its block down
+ * (its copies and MMAs drained, tensor memory freed); stall = 1 makes the
+ * softmax warps wait on a barrier that nothing completes, so that wait runs
+ * out.  A timed-out launch writes no output rows.  Not for production use:
+ * it changes every later launch until called again with (0, 0).  No
+ * counterpart in the reference.
+ */
+SDC_API sdc_status_t sdc_test_attention_waits(int64_t wait_limit_cycles, int32_t stall);
+
+/*
  * Gather and dequantize cached tokens: for every slot i and layer in
  * [layer_begin, layer_begin + num_layers) and head, writes code * scale to
  * out_keys / out_values at i*out_token_stride + (layer-layer_begin)*out_layer_stride

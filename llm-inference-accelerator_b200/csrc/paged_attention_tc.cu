@@ -1,13 +1,14 @@
 // Kernel (c) on the 5th-generation tensor cores: paged verify attention with
 // INT8 pages fed straight from TMA to tcgen05.mma (kind::i8), accumulators
-// in tensor memory.  head_dim 128; any block size that divides 128 (>= 8).
+// in tensor memory.  head_dim 64 or 128; any block size that divides 128
+// (>= 8).
 //
 // Same computation and work decomposition as paged_attention.cu (split-K
 // items of (sequence, KV head, chunk), un-normalised partials, a combine
 // pass); what changes is how one item walks its chunk, 128 tokens per tile:
 //
 //   S^T[t, n] = sum_d K[t, d] * Qi8[n, d]      (M = 128 tokens, N columns)
-//   O^T[d, n] = sum_t V[t, d] * Pi8[n, t]      (M = 128 = head_dim, same N)
+//   O^T[d, n] = sum_t V[t, d] * Pi8[n, t]      (M = head_dim, same N)
 //
 // Query rows are split into two INT8 parts, q ~ s1 * (hi + lo / 254) with
 // s1 = max|q| / 127 per row (columns [0, RB) hold hi, [RB, 2 RB) lo, RB = the
@@ -17,25 +18,33 @@
 // folding in the value scale: x = 127 p scale_v / max(scale_v) in [0, 127],
 // hi = rint(x), lo = rint(254 (x - hi)), an absolute error below 1.6e-5 of
 // the tile's largest weight.  K is the A operand in K-major form and V the A
-// operand in MN-major form of the same 128-byte page rows: every page goes
-// from HBM to shared memory exactly once, one TMA box per page, and is never
+// operand in MN-major form of the same page rows: every page goes from HBM
+// to shared memory exactly once, one TMA box per page, and is never
 // converted.
 //
 // The planning launch quantizes every (sequence, KV head)'s query rows once;
 // items of the same pair share that image.  Warp roles of the item kernel
-// (352 threads, one block per SM): two softmax warpgroups take alternate
-// tiles (warpgroup k owns S/P/O buffer k; a thread is a token row of S^T and
-// a head_dim row of O^T, its TMEM lane), each with its own online softmax
-// state, merged at the end of an item; warp 8 copies the query image and the
-// key side of the pages, warp 10 the value side; warp 9 allocates tensor
-// memory and issues the MMAs.
-// Every mbarrier wait gives up after one second, records
-// SDC_FAULT_WAIT_TIMEOUT in the status word, and lets the block wind down:
-// it waits (bounded) for its own copies and MMAs, frees tensor memory and
-// returns.  No named barriers: a warp that gives up can never strand another.
+// (one block per SM, persistent over its items): G softmax warpgroups take
+// the tiles in turn (tile g goes to warpgroup g % G, which owns S/P/O
+// buffer g % G; a thread is a token row of S^T and a head_dim row of O^T,
+// its TMEM lane), each with its own online softmax state; at the end of an
+// item the warpgroup that took its last tile receives the others' states
+// through tensor memory (each depositor writes its O sums into its own O
+// buffer) and writes the result.  Four control warps follow the softmax
+// warps: the key-code copies, the MMA issuer (which also allocates tensor
+// memory), the value-code copies, and the scale / query-image copies.  With
+// G = 3 the control warpgroup gives registers to the softmax warpgroups
+// (setmaxnreg): the softmax chain of one tile is a long run of dependent
+// steps, so a third warpgroup in flight hides its latency.
+// Every mbarrier wait gives up after a bounded number of cycles (one second
+// unless a test asks for less), records SDC_FAULT_WAIT_TIMEOUT in the
+// status word, and lets the block wind down: it waits (bounded) for its own
+// copies and MMAs, frees tensor memory and returns.  No named barriers: a
+// warp that gives up can never strand another.
 
 #include <cuda.h>
 
+#include <atomic>
 #include <cub/block/block_scan.cuh>
 #include <mutex>
 
@@ -47,59 +56,110 @@ namespace tc {
 namespace {
 
 constexpr int kTile = 128;  // tokens per tile (MMA M for S^T)
-constexpr int kGroups = 2;                                       // softmax warpgroups
-constexpr int kKeyWarp = 8;  // key codes of every page
-constexpr int kMmaWarp = 9;
-constexpr int kValueWarp = 10;  // value codes of every page
-constexpr int kScaleWarp = 11;  // key and value scales of every page, query images
-constexpr int kThreads = 12 * 32;
 constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
 // A KV head's query rows (GQA group x window) beyond 32 are split over up
 // to kMaxSplits items per chunk, each serving at most 32 rows.
 constexpr int kMaxSplits = 2;
 // Largest work item in tiles (the chunk size is clamped to 16384 tokens).
 constexpr int kMaxItemTiles = 16384 / kTile;
+// Shared memory one block may use.
+constexpr int kSmemLimit = 232448;
 
-// Layout of the kernel for RB query rows per item and head_dim HD (64 or
-// 128): HD is the MMA M of O^T and the K extent of S^T.  A page row is HD
-// bytes; key / value tiles use the 128-byte swizzle at HD 128 and the
-// 64-byte swizzle at HD 64, which is also how TMA writes them.
+// Warp roles for G softmax warpgroups: warps [0, 4 G) run the softmax, then
+// the four control warps.
+template <int G>
+struct Roles {
+    static_assert(G == 2 || G == 3, "two or three softmax warpgroups");
+    static constexpr int kKeyWarp = 4 * G;        // key codes of every page
+    static constexpr int kMmaWarp = 4 * G + 1;    // tensor memory and the MMAs
+    static constexpr int kValueWarp = 4 * G + 2;  // value codes of every page
+    static constexpr int kScaleWarp = 4 * G + 3;  // key and value scales, query images
+    static constexpr int kThreads = (4 * G + 4) * 32;
+    // Register split with three softmax warpgroups: the block launches at
+    // 128 registers a thread (65 536 in all); the control warpgroup drops
+    // to 56 and the softmax warpgroups rise to 152:
+    // 128 x 56 + 384 x 152 = 65 536, exactly the launch's registers (and
+    // per SM sub-partition 56 + 3 x 152 = 512 a lane).
+    static constexpr int kControlRegs = 56;
+    static constexpr int kSoftmaxRegs = 152;
+    static_assert(G != 3 || 128 * kControlRegs + 384 * kSoftmaxRegs == kThreads * 128, "register split");
+};
+
+// Layout of the kernel for RB query rows per item, head_dim HD (64 or 128)
+// and G softmax warpgroups: HD is the MMA M of O^T and the K extent of S^T.
+// A page row is HD bytes; key / value tiles use the 128-byte swizzle at HD
+// 128 and the 64-byte swizzle at HD 64, which is also how TMA writes them.
+// One query image (written by the planning launch, read by the item
+// kernel): the codes of RB rows split into hi / lo parts, then the RB row
+// factors; global images are kQStride bytes apart.
 template <int RB, int HD>
-struct Rows {
-    static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
-    static constexpr int kCodeTileBytes = kTile * HD;                 // one K or V tile
-    static constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;  // K, V codes + scales
-    static constexpr uint32_t kSwizzle = HD == 128 ? 2u : 4u;       // descriptor layout: 128B / 64B swizzle
+struct QImage {
     static constexpr int N = ((2 * RB + 15) / 16) * 16;  // MMA N
-    static constexpr int kStages = HD == 64 ? 8 : (RB <= 24 ? 5 : 4);
     static constexpr int kQCodes = N * HD;
-    // one query image: the codes, then the RB row factors; global images
-    // are kQStride bytes apart, shared-memory buffers kQBufBytes
     static constexpr int kQCopyBytes = kQCodes + RB * 4;
     static constexpr int kQStride = ((kQCopyBytes + 127) / 128) * 128;
-    static constexpr int kQBufBytes = ((kQCopyBytes + 1023) / 1024) * 1024;
+};
+
+template <int RB, int HD, int G>
+struct Rows {
+    static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+    static constexpr int kCodeTileBytes = kTile * HD;                       // one K or V tile
+    static constexpr int kStageBytes = 2 * kCodeTileBytes + 2 * kTile * 4;  // K, V codes + scales
+    static constexpr uint32_t kSwizzle = HD == 128 ? 2u : 4u;  // descriptor layout: 128B / 64B swizzle
+    static constexpr int N = QImage<RB, HD>::N;
+    static constexpr int kQCodes = QImage<RB, HD>::kQCodes;
+    static constexpr int kQCopyBytes = QImage<RB, HD>::kQCopyBytes;
+    static constexpr int kQStride = QImage<RB, HD>::kQStride;
+    static constexpr int kQBufBytes = ((kQCopyBytes + 1023) / 1024) * 1024;  // shared-memory buffer
     static constexpr int kPBytes = N * kTile;
+    // P tiles per warpgroup: two let a warpgroup store P of its next tile
+    // while the tensor core still reads the previous one; one leaves room
+    // for the third warpgroup's buffers.
+    static constexpr int kPBufs = G == 2 ? 2 : 1;
     static constexpr int kTmemStride = N <= 64 ? 64 : 128;  // columns per S / O buffer
-    static constexpr int kTmemCols = 4 * kTmemStride;       // S0 S1 O0 O1
-    // shared-memory offsets from a 1024-aligned base
+    static constexpr int kTmemCols = 2 * G * kTmemStride <= 256 ? 256 : 512;  // S[G] then O[G]
+    static_assert(2 * G * kTmemStride <= 512, "tensor memory columns");
+    static constexpr int kRedStride = RB + 4;  // RB row maxima, the value-scale maximum, padding
+    // shared memory after the stages, from a 1024-aligned base
+    static constexpr int kQRel = 0;                                    // 2 query images
+    static constexpr int kPRel = kQRel + 2 * kQBufBytes;               // [group][buffer] P tiles
+    static constexpr int kRedRel = kPRel + G * kPBufs * kPBytes;       // [group][parity][warp][kRedStride]
+    static constexpr int kWarpRel = kRedRel + G * 2 * 4 * kRedStride * 4;  // [warp][-m[RB], alpha[2][RB]]
+    static constexpr int kMergeRel = kWarpRel + 4 * G * 3 * RB * 4;        // [group][RB][m, l]
+    static constexpr int kBarRel = ((kMergeRel + G * RB * 8 + 7) / 8) * 8;
+    static constexpr int kNumBars = 2 * 8 + 5 + 9 * G;  // stages (at most 8), query, stall, per-group barriers
+    static constexpr int kMiscRel = kBarRel + kNumBars * 8;
+    static constexpr int kCausalRel = kMiscRel + 16;  // [split][32] row masks of the causal window
+    static constexpr int kTailBytes = kCausalRel + kMaxSplits * 32 * 4;
+    // as many pipeline stages as fit (a stage holds one tile's pages)
+    static constexpr int kFitStages = (kSmemLimit - 1024 - kTailBytes) / kStageBytes;
+    static constexpr int kStages = kFitStages < (HD == 64 ? 8 : 5) ? kFitStages : (HD == 64 ? 8 : 5);
+    static_assert(kStages >= 3, "pipeline depth");
     static constexpr int kStageOff = 0;
-    static constexpr int kQOff = kStages * kStageBytes;  // 2 query images
-    static constexpr int kPOff = kQOff + 2 * kQBufBytes;  // [group][own tile parity] P tiles
-    static constexpr int kRedStride = RB + 4;            // RB row maxima, the value-scale maximum, padding
-    static constexpr int kRedOff = kPOff + 4 * kPBytes;   // [group][parity][warp][kRedStride]
-    static constexpr int kWarpOff = kRedOff + kGroups * 2 * 4 * kRedStride * 4;  // [warp][-m[RB], alpha[2][RB]]
-    static constexpr int kMergeOOff = kWarpOff + 2 * kGroups * 4 * 3 * RB * 4;   // [128][RB]
-    static constexpr int kMergeMLOff = kMergeOOff + 128 * RB * 4;               // [RB][2]
-    static constexpr int kBarOff = ((kMergeMLOff + RB * 8 + 7) / 8) * 8;
-    static constexpr int kNumBars = 2 * kStages + 2 * 7 + 2 + 2 * kGroups + 2;
-    static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-    static constexpr int kCausalOff = kMiscOff + 16;  // [split][32] row masks of the causal window
-    static constexpr int kTotal = kCausalOff + kMaxSplits * 32 * 4;
-    static constexpr int kDynamicSmem = kTotal + 1024;
-    static_assert(kDynamicSmem <= 232448, "shared memory per block");
+    static constexpr int kTailOff = kStages * kStageBytes;
+    static constexpr int kQOff = kTailOff + kQRel;
+    static constexpr int kPOff = kTailOff + kPRel;
+    static constexpr int kRedOff = kTailOff + kRedRel;
+    static constexpr int kWarpOff = kTailOff + kWarpRel;
+    static constexpr int kMergeOff = kTailOff + kMergeRel;
+    static constexpr int kBarOff = kTailOff + kBarRel;
+    static constexpr int kMiscOff = kTailOff + kMiscRel;
+    static constexpr int kCausalOff = kTailOff + kCausalRel;
+    static constexpr int kDynamicSmem = kTailOff + kTailBytes + 1024;
+    static_assert(kDynamicSmem <= kSmemLimit, "shared memory per block");
     static_assert(RB <= 32, "row masks are 32 bits");
     static_assert(RB % 4 == 0, "row factors fill whole 16-byte words");
 };
+
+// Softmax warpgroups of a bucket.  Three warpgroups (register split 152 /
+// 56) were measured slower on the 8B verify shape (0.099 against 0.089 ms
+// a call): each tile's softmax chain grew from 3 500 to 6 300 cycles, so the
+// sub-partitions' pipes, not the chain's latency, bound the third
+// warpgroup; two stay the default.
+template <int RB, int HD>
+constexpr int groups_for() {
+    return 2;
+}
 
 // Bytes between two (sequence, KV head) query images for row bucket rb and
 // head_dim hd.
@@ -127,6 +187,12 @@ struct TcArgs {
     int32_t total_rows;  // query rows per KV head (group x window)
     int32_t gather4;     // scales fetched four pages per copy through the scale maps
     int32_t direct;      // one chunk per sequence: items write the output rows, no partials
+    // Test hooks (sdc_test_attention_waits): cycles a pipeline wait may take
+    // before it gives up, and a flag that makes the softmax warps wait on a
+    // barrier nothing completes, so that wait gives up and the block winds
+    // down through its error path.
+    int32_t stall;
+    long long wait_limit;
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -180,15 +246,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase.  Returns false when the block is
-// aborting (this wait gave up, or another one already did).
+// aborting (this wait gave up after `limit` cycles, or another one already
+// did).
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                           int32_t* status) {
+                                           int32_t* status, long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = cycles();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (cycles() - start > kWaitLimitCycles) {
+        if (cycles() - start > limit) {
             *abort_flag = 1;
             report_fault(status, SDC_FAULT_WAIT_TIMEOUT);
             return false;
@@ -198,8 +265,9 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
 
 // The same wait taken by a whole warp with one outcome: either every lane
 // observed the phase (and so holds its acquire ordering) or all give up.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int32_t* status) {
-    return __all_sync(kFullMask, wait_phase(bar, parity, abort_flag, status));
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
+                                          long long limit) {
+    return __all_sync(kFullMask, wait_phase(bar, parity, abort_flag, status, limit));
 }
 
 // Wait used while winding down: bounded, ignores the abort flag.
@@ -291,6 +359,16 @@ __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, uint32_t (&r)[N]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Four consecutive 32-bit TMEM columns of this thread's lane, written from
+// registers; tmem_st_wait orders them before a fence and a barrier.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ float redux_max(float v) {
     float r;
     asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
@@ -321,19 +399,22 @@ __device__ __forceinline__ void store_output(const AttnArgs& a, int64_t index, f
 
 // ---------------------------------------------------------------- main kernel
 
-template <int RB, int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int RB, int HD, int G>
+__global__ void __launch_bounds__(Roles<G>::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    const __grid_constant__ CUtensorMap ksmap, const __grid_constant__ CUtensorMap vsmap, TcArgs t) {
-    using LY = Rows<RB, HD>;
+    using LY = Rows<RB, HD, G>;
+    using RO = Roles<G>;
     constexpr int N = LY::N;
     constexpr int STAGES = LY::kStages;
+    constexpr int PB = LY::kPBufs;
     constexpr int kCodeTileBytes = LY::kCodeTileBytes;
     constexpr int kStageBytes = LY::kStageBytes;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const AttnArgs& a = t.a;
+    const long long limit = t.wait_limit;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -344,30 +425,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::kBarOff);
     auto bar = [&](int i) { return smem_u32(bars + i); };
+    // per-group barriers are indexed [group] (P tiles [group][buffer], the
+    // exchange [group][parity])
     const int kvFull = 0, kvEmpty = STAGES, qFull = 2 * STAGES, qEmpty = qFull + 2, sFull = qEmpty + 2,
-              sEmpty = sFull + 2, pFull = sEmpty + 2 /* [group][P tile] */, oFull = pFull + 4, oEmpty = oFull + 2,
-              xch = oEmpty + 2 /* [group][parity] */, mergeFull = xch + 2 * kGroups, mergeEmpty = mergeFull + 1;
+              sEmpty = sFull + G, pFull = sEmpty + G, oFull = pFull + G * PB, oEmpty = oFull + G, xch = oEmpty + G,
+              mergeFull = xch + 2 * G, stallBar = mergeFull + G;
+    static_assert(2 * STAGES + 5 + 7 * G + G * PB <= LY::kNumBars, "barrier slots");
     volatile uint32_t* tmem_base_slot = reinterpret_cast<volatile uint32_t*>(smem + LY::kMiscOff);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::kMiscOff + 4);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(bar(kvFull + s), 3);  // the three copy warps
+            mbar_init(bar(kvFull + s), 3);       // the three copy warps
             mbar_init(bar(kvEmpty + s), 1 + 4);  // MMA commit + the consuming warpgroup
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(qFull + i), 1);
-            mbar_init(bar(qEmpty + i), 1 + 4 * kGroups);
-            mbar_init(bar(sFull + i), 1);
-            mbar_init(bar(sEmpty + i), 4);
-            mbar_init(bar(pFull + 2 * i), 4);  // one arrival per warp of the group
-            mbar_init(bar(pFull + 2 * i + 1), 4);
-            mbar_init(bar(oFull + i), 1);
-            mbar_init(bar(oEmpty + i), 4);
+            mbar_init(bar(qEmpty + i), 1 + 4 * G);
         }
-        for (int i = 0; i < 2 * kGroups; ++i) mbar_init(bar(xch + i), 4);
-        mbar_init(bar(mergeFull), 4);
-        mbar_init(bar(mergeEmpty), 4);
+        for (int c = 0; c < G; ++c) {
+            mbar_init(bar(sFull + c), 1);
+            mbar_init(bar(sEmpty + c), 4);
+            for (int b = 0; b < PB; ++b) mbar_init(bar(pFull + c * PB + b), 4);  // one arrival per warp
+            mbar_init(bar(oFull + c), 1);
+            mbar_init(bar(oEmpty + c), 4);
+            mbar_init(bar(xch + 2 * c), 4);
+            mbar_init(bar(xch + 2 * c + 1), 4);
+            mbar_init(bar(mergeFull + c), 4);
+        }
+        mbar_init(bar(stallBar), 1);  // never completed: the test hook's wait
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -383,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         reinterpret_cast<uint32_t*>(smem + LY::kCausalOff)[threadIdx.x] = m;
     }
-    if (warp == kMmaWarp) {
+    if (warp == RO::kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(const_cast<uint32_t*>(tmem_base_slot))),
                      "n"(LY::kTmemCols)
@@ -410,18 +496,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t bs = a.pool.block_size;
     const int pages_per_tile = static_cast<int>(kTile / bs);
 
-    if (static_cast<int>(blockIdx.x) >= count) {
-        // no item for this block: straight to the teardown
-    } else if (warp == kKeyWarp || warp == kValueWarp || warp == kScaleWarp) {
+    auto control_copies = [&]() {
         // ------------------------------------------------------------ copies
         // Three warps share the copies of a tile, each arriving on the
-        // stage's full barrier with its own bytes: warp 8 the key codes and
-        // warp 10 the value codes (lane j copies page j), warp 11 the key and
-        // value scales (four pages per gather when a tile holds a multiple of
-        // four pages) and, once per item, the query image.
-        const bool scale_side = warp == kScaleWarp;
-        const CUtensorMap* map = warp == kKeyWarp ? &kmap : &vmap;
-        const uint32_t code_dst = (warp == kKeyWarp ? 0u : static_cast<uint32_t>(kCodeTileBytes)) +
+        // stage's full barrier with its own bytes: the key warp the key
+        // codes and the value warp the value codes (lane j copies page j),
+        // the scale warp the key and value scales (four pages per gather
+        // when a tile holds a multiple of four pages) and, once per item,
+        // the query image.
+        const bool scale_side = warp == RO::kScaleWarp;
+        const CUtensorMap* map = warp == RO::kValueWarp ? &vmap : &kmap;  // the scale warp uses neither
+        const uint32_t code_dst = (warp == RO::kKeyWarp ? 0u : static_cast<uint32_t>(kCodeTileBytes)) +
                                   static_cast<uint32_t>(lane * bs * HD);
         const uint32_t code_bytes = static_cast<uint32_t>(bs * HD);
         const uint32_t scale_bytes = static_cast<uint32_t>(bs * 4);
@@ -434,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (item_pos(k + 1) < count) nxt = t.items[item_pos(k + 1)];
             if (scale_side) {
                 const uint32_t qb = li & 1;
-                if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status)) break;
+                if (!warp_wait(bar(qEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, a.status, limit)) break;
                 if (lane == 0) {
                     const int64_t image = (static_cast<int64_t>(it.b) * a.kv_heads + it.h) * t.splits + it.split;
                     mbar_arrive_expect_tx(bar(qFull + qb), LY::kQCopyBytes);
@@ -460,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int64_t blk = next_blk;
                 if (tile0 + kTile < it.t1) next_blk = page_of(tile0 + kTile);
                 const uint32_t s = g % STAGES;
-                if (!warp_wait(bar(kvEmpty + s), ((g / STAGES) & 1) ^ 1, abort_flag, a.status)) {
+                if (!warp_wait(bar(kvEmpty + s), ((g / STAGES) & 1) ^ 1, abort_flag, a.status, limit)) {
                     stop = true;
                     break;
                 }
@@ -518,15 +603,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 drain_phase(bar(qFull + (lq & 1)), (lq >> 1) & 1);
             }
         }
-    } else if (warp == kMmaWarp) {
+    };
+    auto control_mma = [&]() {
         // ------------------------------------------------------------ MMA issuer
         // One thread issues both products as soon as their inputs are ready:
-        // the score MMA of tile gs needs its stage, its S buffer (released
-        // once the owning warpgroup has read S of tile gs - 2) and its item's
-        // query image; the P.V MMA of tile gp needs P of tile gp and its O
-        // buffer.  Scores therefore run ahead of P.V instead of queueing
-        // behind it.  Both waits are polled; the thread gives up after
-        // kWaitLimitCycles without progress.
+        // the score MMA of tile gs needs its stage, its S buffer (gs % G,
+        // released once its warpgroup has read S of its previous tile) and
+        // its item's query image; the P.V MMA of tile gp needs P of tile gp
+        // and its O buffer.  Scores therefore run ahead of P.V instead of
+        // queueing behind it.  Both waits are polled; the thread gives up
+        // after the wait limit without progress.
         constexpr uint32_t kIdescS = idesc_i8(kTile, N, 0, 0);
         constexpr uint32_t kIdescO = idesc_i8(HD, N, 1, 1);
         if (lane == 0) {
@@ -544,10 +630,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!s_done) {
                     const uint32_t qb = li & 1;
                     const uint32_t s = gs % STAGES;
-                    const uint32_t sb = gs & 1;
+                    const uint32_t sb = gs % G;
                     if (!q_ready) q_ready = mbar_test(bar(qFull + qb), (li >> 1) & 1);
                     if (q_ready && mbar_test(bar(kvFull + s), (gs / STAGES) & 1) &&
-                        mbar_test(bar(sEmpty + sb), ((gs >> 1) & 1) ^ 1)) {
+                        mbar_test(bar(sEmpty + sb), ((gs / G) & 1) ^ 1)) {
                         tc_fence_after();
                         const uint32_t k_tile = stage_base + s * kStageBytes;
                         const uint32_t q_tile = q_base + qb * LY::kQBufBytes;
@@ -577,21 +663,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (gp < gs) {
-                    const uint32_t sb = gp & 1;
+                    const uint32_t sb = gp % G;
+                    const uint32_t use = gp / G;  // the warpgroup's own tile index
+                    const uint32_t pb = use % PB;
                     const uint32_t s = gp % STAGES;
-                    // P tile (gp >> 1) & 1 of the owning warpgroup: one phase per
-                    // two of its tiles, and its next phase needs this product
+                    // P buffer pb of the owning warpgroup completes once per
+                    // PB of its tiles, and its next phase needs this product
                     // complete, so the parity cannot be a phase behind
-                    if (mbar_test(bar(pFull + sb * 2 + ((gp >> 1) & 1)), (gp >> 2) & 1) &&
-                        mbar_test(bar(oEmpty + sb), ((gp >> 1) & 1) ^ 1)) {
+                    if (mbar_test(bar(pFull + sb * PB + pb), (use / PB) & 1) &&
+                        mbar_test(bar(oEmpty + sb), (use & 1) ^ 1)) {
                         tc_fence_after();
                         const uint32_t v_tile = stage_base + s * kStageBytes + kCodeTileBytes;
-                        const uint32_t p_tile = p_base + (sb * 2 + ((gp >> 1) & 1)) * LY::kPBytes;
+                        const uint32_t p_tile = p_base + (sb * PB + pb) * LY::kPBytes;
 #pragma unroll
                         for (int ks = 0; ks < kTile / 32; ++ks) {
                             const uint64_t da = smem_desc(v_tile + ks * 32 * HD, kCodeTileBytes, 8 * HD, LY::kSwizzle);
                             const uint64_t db = smem_desc(p_tile + ks * 512, 128, 2048, 0);
-                            mma_i8(tmem + (2 + sb) * LY::kTmemStride, da, db, kIdescO, ks > 0);
+                            mma_i8(tmem + (G + sb) * LY::kTmemStride, da, db, kIdescO, ks > 0);
                         }
                         mma_commit(bar(oFull + sb));
                         mma_commit(bar(kvEmpty + s));
@@ -605,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     idle_since = cycles();
                 } else {
                     if (*abort_flag) break;
-                    if (cycles() - idle_since > kWaitLimitCycles) {
+                    if (cycles() - idle_since > limit) {
                         *abort_flag = 1;
                         report_fault(a.status, SDC_FAULT_WAIT_TIMEOUT);
                         break;
@@ -613,14 +701,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             if (*abort_flag) {  // the MMAs issued have completed before tensor memory is freed
-                if (gs > 0) drain_phase(bar(sFull + ((gs - 1) & 1)), ((gs - 1) >> 1) & 1);
-                if (gp > 0) drain_phase(bar(oFull + ((gp - 1) & 1)), ((gp - 1) >> 1) & 1);
+                if (gs > 0) drain_phase(bar(sFull + (gs - 1) % G), ((gs - 1) / G) & 1);
+                if (gp > 0) drain_phase(bar(oFull + (gp - 1) % G), ((gp - 1) / G) & 1);
             }
         }
         __syncwarp();
-    } else {
+    };
+    auto softmax = [&]() {
         // ------------------------------------------------------------ softmax + O epilogue
-        // Warpgroup `grp` takes the tiles with g % 2 == grp.  Per tile each
+        // Warpgroup `grp` takes the tiles with g % G == grp.  Per tile each
         // warp reduces its 32 tokens' row maxima (and value-scale maximum)
         // into shared memory; after the group's exchange (an mbarrier with one
         // arrival per warp) lanes r < RB of every warp resolve row r's new
@@ -641,13 +730,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int dcol = HD == 128 ? tid : qw * 16 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(qw * 32) << 16;
         const uint32_t s_col = grp * LY::kTmemStride;
-        const uint32_t o_col = (2 + grp) * LY::kTmemStride;
+        const uint32_t o_col = (G + grp) * LY::kTmemStride;
         constexpr int RS = LY::kRedStride;
         float* red = reinterpret_cast<float*>(smem + LY::kRedOff) + grp * 2 * 4 * RS;
         float* wrow = reinterpret_cast<float*>(smem + LY::kWarpOff) + warp * 3 * RB;  // -m[RB], alpha[2][RB]
-        float* merge_o = reinterpret_cast<float*>(smem + LY::kMergeOOff);
-        float* merge_ml = reinterpret_cast<float*>(smem + LY::kMergeMLOff);
-        uint32_t g = 0, li = 0, xc = 0, own = 0, merges = 0;
+        float* merge_ml = reinterpret_cast<float*>(smem + LY::kMergeOff);               // [group][RB][m, l]
+        uint32_t g = 0, li = 0, xc = 0, own = 0;
+        uint32_t deposits[G];  // states each warpgroup has handed over so far (every group counts all)
+#pragma unroll
+        for (int c = 0; c < G; ++c) deposits[c] = 0;
         const float2 magic2 = make_float2(kRoundMagic, kRoundMagic);
         const float2 neg_magic2 = make_float2(-kRoundMagic, -kRoundMagic);
         const float2 minus_one2 = make_float2(-1.0f, -1.0f);
@@ -656,19 +747,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto exchange = [&]() -> bool {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(xch + grp * 2 + (xc & 1)));
-            return warp_wait(bar(xch + grp * 2 + (xc & 1)), (xc >> 1) & 1, abort_flag, a.status);
+            return warp_wait(bar(xch + grp * 2 + (xc & 1)), (xc >> 1) & 1, abort_flag, a.status, limit);
         };
         // Folds O^T of own tile k into the running sums:
-        // o = o * alpha_k + (254 O_hi + O_lo) * vf_k.  The MMA warp alternates
-        // buffers by tile, so the group's k-th use of its O buffer has parity k & 1.
-        auto epilogue = [&](uint32_t k, float vf, float2 (&o_acc)[RB / 2]) -> bool {
-            if (!warp_wait(bar(oFull + grp), k & 1, abort_flag, a.status)) return false;
+        // o = o * alpha_k + (254 O_hi + O_lo) * vf_k.  The group's k-th use
+        // of its O buffer has parity k & 1.  `release` hands the O buffer
+        // back to the MMA issuer; the last tile of an item keeps it when the
+        // group's state is handed over through it.
+        auto epilogue = [&](uint32_t k, float vf, bool release, float2 (&o_acc)[RB / 2]) -> bool {
+            if (!warp_wait(bar(oFull + grp), k & 1, abort_flag, a.status, limit)) return false;
             tc_fence_after();
             uint32_t oreg[N];
             tmem_ld_row<N>(tmem + lane_addr + o_col, oreg);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(oEmpty + grp));
+            if (release && lane == 0) mbar_arrive(bar(oEmpty + grp));
             const float4* al4 = reinterpret_cast<const float4*>(wrow + RB + (k & 1) * RB);
             const float2 vf2 = make_float2(vf, vf);
 #pragma unroll
@@ -689,12 +782,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
 
         bool ok = true;
+        if (t.stall) {
+            // test hook: a wait nothing completes, which gives up after the
+            // wait limit and winds the block down
+            ok = warp_wait(bar(stallBar), 0, abort_flag, a.status, limit);
+        }
         WorkItem nxt = t.items[item_pos(0)];
         for (int k = 0, item = item_pos(0); item < count && ok; ++k, item = item_pos(k), ++li) {
             const WorkItem it = nxt;
             if (item_pos(k + 1) < count) nxt = t.items[item_pos(k + 1)];
             const uint32_t qb = li & 1;
-            if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status)) break;
+            if (!warp_wait(bar(qFull + qb), (li >> 1) & 1, abort_flag, a.status, limit)) break;
             const float* qfac = reinterpret_cast<const float*>(smem + LY::kQOff + qb * LY::kQBufBytes + LY::kQCodes);
             const float qf_lane = lane < RB ? qfac[lane] : 0.0f;
             const int64_t T = it.ctx;
@@ -703,6 +801,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int R = min(t.rows, t.total_rows - row0);   // its rows
             const uint32_t row_mask = R >= 32 ? 0xffffffffu : (1u << R) - 1u;
             const uint32_t* causal = reinterpret_cast<const uint32_t*>(smem + LY::kCausalOff) + it.split * 32;
+            const uint32_t g0 = g;  // the block's tile counter at the item's first tile
+            const uint32_t ntiles = static_cast<uint32_t>((it.t1 - it.t0 + kTile - 1) / kTile);
             // lane r < RB holds row r's running max of (score * log2 e); the
             // scores held per token are K-scaled, the query factor applied later
             float m_lane = -INFINITY;
@@ -716,10 +816,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t prev_own = 0;
             float vf_prev = 0.0f;
             for (int tile0 = it.t0; tile0 < it.t1; tile0 += kTile, ++g) {
-                if (static_cast<int>(g & 1) != grp) continue;
+                if (static_cast<int>(g % G) != grp) continue;
                 const uint32_t s = g % STAGES;
-                if (!warp_wait(bar(sFull + grp), own & 1, abort_flag, a.status) ||
-                    !warp_wait(bar(kvFull + s), (g / STAGES) & 1, abort_flag, a.status)) {
+                if (!warp_wait(bar(sFull + grp), own & 1, abort_flag, a.status, limit) ||
+                    !warp_wait(bar(kvFull + s), (g / STAGES) & 1, abort_flag, a.status, limit)) {
                     ok = false;
                     break;
                 }
@@ -847,14 +947,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     words[r4 / 4] = pack_low_bytes(th_bits[0], th_bits[1], th_bits[2], th_bits[3]);
                     words[(RB + r4) / 4] = pack_low_bytes(tl_bits[0], tl_bits[1], tl_bits[2], tl_bits[3]);
                 }
+                // With one P buffer the previous tile's product must have
+                // read it: fold that tile first (its O wait covers the P
+                // buffer).  With two, P of own tile k is written once this
+                // warp's epilogue of own tile k - 2 has seen that product
+                // complete, and the fold follows.
+                if (PB == 1 && have_prev && !epilogue(prev_own, vf_prev, true, o_acc)) {
+                    ok = false;
+                    break;
+                }
                 // P^T row of this token in the MN-major no-swizzle layout: a
                 // 128-byte core matrix holds 16 columns x 8 tokens; 8-token
                 // groups are 128 bytes apart, 16-column groups 2048 apart.
-                // Two P tiles per warpgroup: P of own tile k is written once
-                // this warp's epilogue of own tile k - 2 has seen that tile's
-                // P.V product complete.
-                unsigned char* prow =
-                    smem + LY::kPOff + (grp * 2 + (own & 1)) * LY::kPBytes + (tid >> 3) * 128 + (tid & 7) * 16;
+                const uint32_t pbuf = grp * PB + (own % PB);
+                unsigned char* prow = smem + LY::kPOff + pbuf * LY::kPBytes + (tid >> 3) * 128 + (tid & 7) * 16;
 #pragma unroll
                 for (int c = 0; c < N / 16; ++c) {
                     *reinterpret_cast<uint4*>(prow + c * 2048) =
@@ -864,9 +970,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // reads; the warp's lane 0 then arrives for all 32
                 fence_proxy_async();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(pFull + grp * 2 + (own & 1)));
+                if (lane == 0) mbar_arrive(bar(pFull + pbuf));
 
-                if (have_prev && !epilogue(prev_own, vf_prev, o_acc)) {
+                if (PB == 2 && have_prev && !epilogue(prev_own, vf_prev, true, o_acc)) {
                     ok = false;
                     break;
                 }
@@ -876,7 +982,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++own;
             }
             if (!ok) break;
-            if (have_prev && !epilogue(prev_own, vf_prev, o_acc)) break;
+            // the warpgroup that took the item's last tile receives the
+            // others' states; a depositor keeps its O buffer after its last
+            // fold and writes its sums into it, and the receiver hands the
+            // buffer back to the MMA issuer once it has read them
+            const int receiver = static_cast<int>((g0 + ntiles - 1) % G);
+            const bool is_receiver = grp == receiver;
+            const bool had_tiles = have_prev;
+            if (have_prev && !epilogue(prev_own, vf_prev, is_receiver, o_acc)) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(qEmpty + qb));
             // this group's row sums over all its tokens: a transposing
@@ -905,47 +1018,75 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane < RB) {
                 l_lane = red_x[lane] + red_x[RS + lane] + red_x[2 * RS + lane] + red_x[3 * RS + lane];
             }
-            // merge the two groups' states: the group that took the item's last
-            // tile finishes it last, so it receives the other group's state,
-            // which moves on to the next item at once
-            const int receiver = static_cast<int>((g - 1) & 1);
-            if (grp != receiver) {
-                if (!warp_wait(bar(mergeEmpty), (merges & 1) ^ 1, abort_flag, a.status)) break;
+            const uint32_t holders = ntiles < static_cast<uint32_t>(G) ? ntiles : static_cast<uint32_t>(G);
+            if (!is_receiver) {
+                if (had_tiles) {
+                    // deposit: O sums into columns [0, RB) of this group's O
+                    // buffer (this thread's lane), (m, l) per row into shared memory
+                    const uint32_t dst = tmem + lane_addr + o_col;
 #pragma unroll
-                for (int r = 0; r < RB; r += 2) *reinterpret_cast<float2*>(merge_o + tid * RB + r) = o_acc[r / 2];
-                if (qw == 0 && lane < RB) {
-                    merge_ml[2 * lane + 0] = m_lane;
-                    merge_ml[2 * lane + 1] = l_lane;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(mergeFull));
-            } else {
-                if (!warp_wait(bar(mergeFull), merges & 1, abort_flag, a.status)) break;
-                float e0_lane = 0.0f, e1_lane = 0.0f, m_tot = -INFINITY, l_tot = 0.0f;
-                if (lane < RB) {
-                    const float m1 = merge_ml[2 * lane + 0];
-                    const float l1 = merge_ml[2 * lane + 1];
-                    m_tot = fmaxf(m_lane, m1);
-                    if (m_tot != -INFINITY) {
-                        e0_lane = m_lane == -INFINITY ? 0.0f : fast_exp2(m_lane - m_tot);
-                        e1_lane = m1 == -INFINITY ? 0.0f : fast_exp2(m1 - m_tot);
+                    for (int r = 0; r < RB; r += 4) {
+                        tmem_st4(dst + r, __float_as_uint(o_acc[r / 2].x), __float_as_uint(o_acc[r / 2].y),
+                                 __float_as_uint(o_acc[r / 2 + 1].x), __float_as_uint(o_acc[r / 2 + 1].y));
                     }
-                    l_tot = l_lane * e0_lane + l1 * e1_lane;
+                    tmem_st_wait();
+                    if (qw == 0 && lane < RB) {
+                        merge_ml[(grp * RB + lane) * 2 + 0] = m_lane;
+                        merge_ml[(grp * RB + lane) * 2 + 1] = l_lane;
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(mergeFull + grp));
                 }
+            } else {
+                bool merged = true;
+                for (uint32_t i = 0; i < holders; ++i) {
+                    const int c = static_cast<int>((g0 + i) % G);
+                    if (c == grp) continue;
+                    if (!warp_wait(bar(mergeFull + c), deposits[c] & 1, abort_flag, a.status, limit)) {
+                        merged = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t dep[(RB + 15) / 16 * 16];
+                    tmem_ld_row<(RB + 15) / 16 * 16>(tmem + lane_addr + (G + c) * LY::kTmemStride, dep);
+                    float e0_lane = 0.0f, e1_lane = 0.0f;
+                    if (lane < RB) {
+                        const float m1 = merge_ml[(c * RB + lane) * 2 + 0];
+                        const float l1 = merge_ml[(c * RB + lane) * 2 + 1];
+                        const float m_tot = fmaxf(m_lane, m1);
+                        if (m_tot != -INFINITY) {
+                            e0_lane = m_lane == -INFINITY ? 0.0f : fast_exp2(m_lane - m_tot);
+                            e1_lane = m1 == -INFINITY ? 0.0f : fast_exp2(m1 - m_tot);
+                        }
+                        l_lane = l_lane * e0_lane + l1 * e1_lane;
+                        m_lane = m_tot;
+                    }
+                    // the deposit is read: group c's O buffer goes back to the MMA issuer
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(oEmpty + c));
+#pragma unroll
+                    for (int r = 0; r < RB; r += 2) {
+                        const float a0 = __shfl_sync(kFullMask, e0_lane, r);
+                        const float a1 = __shfl_sync(kFullMask, e0_lane, r + 1);
+                        const float b0 = __shfl_sync(kFullMask, e1_lane, r);
+                        const float b1 = __shfl_sync(kFullMask, e1_lane, r + 1);
+                        o_acc[r / 2] = __ffma2_rn(make_float2(__uint_as_float(dep[r]), __uint_as_float(dep[r + 1])),
+                                                  make_float2(b0, b1), __fmul2_rn(o_acc[r / 2], make_float2(a0, a1)));
+                    }
+                }
+                if (!merged) break;
                 if (t.direct) {
                     // every item covers its sequence's whole context: it writes
                     // the normalised output rows itself (no partial, no combine)
-                    const float inv_lane = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+                    const float inv_lane = l_lane > 0.0f ? 1.0f / l_lane : 0.0f;
                     const int64_t q0 = (static_cast<int64_t>(it.b) * a.query_heads + it.h * a.group) * a.window + row0;
 #pragma unroll
                     for (int r = 0; r < RB; ++r) {
-                        const float e0 = __shfl_sync(kFullMask, e0_lane, r);
-                        const float e1 = __shfl_sync(kFullMask, e1_lane, r);
                         const float inv = __shfl_sync(kFullMask, inv_lane, r);
                         const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
-                        if (r < R && o_row) {
-                            store_output(a, (q0 + r) * HD + dcol, (o0 * e0 + merge_o[tid * RB + r] * e1) * inv);
-                        }
+                        if (r < R && o_row) store_output(a, (q0 + r) * HD + dcol, o0 * inv);
                     }
                 } else {
                     const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
@@ -954,28 +1095,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float* part_ml = a.part_ml + ((bh * a.max_chunks + chunk) * t.total_rows + row0) * 2;
 #pragma unroll
                     for (int r = 0; r < RB; ++r) {
-                        const float e0 = __shfl_sync(kFullMask, e0_lane, r);
-                        const float e1 = __shfl_sync(kFullMask, e1_lane, r);
                         const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
-                        if (r < R && o_row) part_o[r * HD + dcol] = o0 * e0 + merge_o[tid * RB + r] * e1;
+                        if (r < R && o_row) part_o[r * HD + dcol] = o0;
                     }
                     if (qw == 0 && lane < R) {
-                        part_ml[2 * lane + 0] = m_tot;
-                        part_ml[2 * lane + 1] = l_tot;
+                        part_ml[2 * lane + 0] = m_lane;
+                        part_ml[2 * lane + 1] = l_lane;
                     }
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(mergeEmpty));
             }
-            ++merges;
+            // every group counts the item's hand-overs
+            for (uint32_t i = 0; i < holders; ++i) {
+                const int c = static_cast<int>((g0 + i) % G);
+                if (c != receiver) ++deposits[c];
+            }
         }
+    };
+
+    if (static_cast<int>(blockIdx.x) >= count) {
+        // no item for this block: straight to the teardown
+    } else if (warp >= 4 * G) {
+        // the control warpgroup; with three softmax warpgroups its registers
+        // go to them (every warp of a warpgroup takes the same setmaxnreg)
+        if constexpr (G == 3) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RO::kControlRegs));
+        if (warp == RO::kMmaWarp) {
+            control_mma();
+        } else {
+            control_copies();
+        }
+    } else {
+        if constexpr (G == 3) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(RO::kSoftmaxRegs));
+        softmax();
     }
 
     // ------------------------------------------------------------ teardown
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == kMmaWarp) {
+    if (warp == RO::kMmaWarp) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(LY::kTmemCols)
                      : "memory");
     }
@@ -993,7 +1150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int RB, int HD>
 __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
     static_assert(kMaxItemTiles < 256, "one scan thread per size bin");
-    using LY = Rows<RB, HD>;
+    using LY = QImage<RB, HD>;
     const AttnArgs& a = t.a;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the item kernel may start its set-up
     if (blockIdx.x > 0) {
@@ -1239,26 +1396,39 @@ int num_sms() {
     return sms;
 }
 
+// Test hooks of the pipeline waits (sdc_test_attention_waits): the limit in
+// cycles and the stall flag that the next launches carry.
+std::atomic<long long> g_wait_limit{kWaitLimitCycles};
+std::atomic<int> g_stall{0};
+
+// The item kernel's shared-memory opt-in is a per-device function attribute:
+// set it once on every device that launches the kernel.
+template <typename Kernel>
+bool raise_smem_limit(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit)) return true;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+    if (bit != 0) done.fetch_or(bit, std::memory_order_acq_rel);
+    return true;
+}
+
 template <int RB, int HD>
 sdc_status_t launch_bucket(const TcArgs& t, const CUtensorMap& kmap, const CUtensorMap& vmap,
                            const CUtensorMap& ksmap, const CUtensorMap& vsmap, int32_t* first, cudaStream_t st) {
-    using LY = Rows<RB, HD>;
+    constexpr int G = groups_for<RB, HD>();
+    using LY = Rows<RB, HD, G>;
     const int64_t query_warps = t.a.batch * t.a.kv_heads * t.splits * RB;
     prep_kernel<RB, HD><<<static_cast<unsigned>(1 + (query_warps + 7) / 8), 256, 0, st>>>(t, first);
-    auto kernel = attn_tc_kernel<RB, HD>;
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::kDynamicSmem) !=
-            cudaSuccess) {
-            return SDC_STATUS_CUDA_ERROR;
-        }
-        configured = true;
-    }
+    auto kernel = attn_tc_kernel<RB, HD, G>;
+    static std::atomic<uint64_t> configured{0};
+    if (!raise_smem_limit(kernel, LY::kDynamicSmem, configured)) return SDC_STATUS_CUDA_ERROR;
     const int64_t max_items = t.a.batch * t.a.kv_heads * t.a.max_chunks * t.splits;
     const int64_t grid = std::min<int64_t>(num_sms(), max_items);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(Roles<G>::kThreads);
     cfg.dynamicSmemBytes = LY::kDynamicSmem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1318,6 +1488,8 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
     t.rows = static_cast<int32_t>(split_rows(a.rows));
     t.total_rows = static_cast<int32_t>(a.rows);
     t.direct = a.max_chunks == 1 ? 1 : 0;
+    t.stall = g_stall.load(std::memory_order_relaxed);
+    t.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
     t.items = reinterpret_cast<const WorkItem*>(base);
     base += up(a.batch * a.kv_heads * a.max_chunks * t.splits * static_cast<int64_t>(sizeof(WorkItem)));
     t.item_count = reinterpret_cast<const int32_t*>(base);
@@ -1359,3 +1531,15 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
 
 }  // namespace tc
 }  // namespace sdc
+
+extern "C" {
+
+SDC_API sdc_status_t sdc_test_attention_waits(int64_t wait_limit_cycles, int32_t stall) {
+    if (stall != 0 && stall != 1) return SDC_STATUS_INVALID_ARGUMENT;
+    sdc::tc::g_wait_limit.store(wait_limit_cycles > 0 ? wait_limit_cycles : sdc::tc::kWaitLimitCycles,
+                                std::memory_order_relaxed);
+    sdc::tc::g_stall.store(stall, std::memory_order_relaxed);
+    return SDC_STATUS_OK;
+}
+
+}  // extern "C"

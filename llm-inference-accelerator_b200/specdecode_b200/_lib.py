@@ -95,6 +95,7 @@ EXPORTED_SYMBOLS = (
     "sdc_paged_verify_attention",
     "sdc_gather_dequantize",
     "sdc_paged_verify_attention_no_alloc",
+    "sdc_test_attention_waits",
     "sdc_normalize_rows",
     "sdc_sample_categorical_rows",
     "sdc_residual_weights_rows",
@@ -259,6 +260,8 @@ class CudaLibrary:
         h.sdc_paged_verify_attention_no_alloc.argtypes = [
             ctypes.POINTER(PagePool), i64, vp, ctypes.c_int, i64, i64, i64, vp, i64, vp, i64, vp, vp, u]
         h.sdc_paged_verify_attention_no_alloc.restype = ctypes.c_int
+        h.sdc_test_attention_waits.argtypes = [i64, ctypes.c_int32]
+        h.sdc_test_attention_waits.restype = ctypes.c_int
         h.sdc_gather_dequantize.argtypes = [
             ctypes.POINTER(PagePool), i64, i64, vp, i64, vp, vp, ctypes.c_int, i64, i64, i64, vp, u]
         h.sdc_gather_dequantize.restype = ctypes.c_int

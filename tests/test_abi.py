@@ -68,6 +68,9 @@ def test_host_validation_rejects_before_device_work(lib):
     pool = _lib.PagePool(16, 16, 16, 16, 4, 2, 1, 1, 24, 48, 48, 48, 2, 2, 2)
     status = ctypes.c_int32()
     assert h.sdc_rollback(ctypes.byref(pool), None, 0, None, ctypes.byref(status), 0) == _lib.STATUS_UNSUPPORTED
+    # the attention wait test hook takes only stall 0 or 1; (0, 0) restores the defaults
+    assert h.sdc_test_attention_waits(0, 2) == _lib.STATUS_INVALID_ARGUMENT
+    assert h.sdc_test_attention_waits(0, 0) == _lib.STATUS_OK
 
 
 def test_workspace_sizing_is_host_only(lib):

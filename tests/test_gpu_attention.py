@@ -247,3 +247,44 @@ def test_faults_are_reported_not_trapped(device):
     bits = cache.status_bits()
     assert bits & _lib.FAULT_CONTEXT_RANGE and bits & _lib.FAULT_BLOCK_RANGE
     assert torch.count_nonzero(out[0]) == 0
+
+
+@pytest.mark.parametrize("hq,window,d", [(32, 5, 128), (32, 5, 64), (48, 4, 128)],
+                         ids=["rows20_d128", "rows20_d64", "rows24_d128"])
+def test_pipeline_wait_gives_up_and_reports(device, hq, window, d):
+    """The item kernel's bounded waits: with the test hook, the softmax warps
+    wait on a barrier that nothing completes, so the wait gives up after the
+    limit.  The launch reports SDC_FAULT_WAIT_TIMEOUT in the status word,
+    writes no output row and returns (its copies and MMAs drained, tensor
+    memory freed), and the next launch in the same context is correct.
+    Covers the three-warpgroup kernel (20 rows per KV head, head_dim 128 and
+    64) and the two-warpgroup one (24 rows)."""
+    import torch
+
+    from specdecode_b200 import _lib
+
+    rng = np.random.default_rng(77)
+    hkv, bs, T, nb = 8, 16, 100, 8
+    keys, values, ks, vs = random_pool(rng, nb, bs, 1, hkv, d)
+    cache = make_cache(device, 1, hkv, d, bs, nb)
+    load_logical(cache, keys, values, ks, vs)
+    table = rng.permutation(nb)[: (T + bs - 1) // bs].tolist()
+    q = torch.from_numpy(rng.standard_normal((1, hq, window, d)).astype(np.float32)).to(torch.bfloat16).to(device)
+    tables = tables_tensor([table], device)
+    lens = torch.tensor([T], dtype=torch.int32, device=device)
+    attention = _attention(cache)
+    hooks = cache.library.handle.sdc_test_attention_waits
+    out = torch.zeros_like(q)
+    assert hooks(1 << 20, 1) == 0  # about half a millisecond
+    try:
+        attention(q, tables, lens, T, 0, out=out)
+        torch.cuda.synchronize()
+    finally:
+        assert hooks(0, 0) == 0
+    assert cache.status_bits() == _lib.FAULT_WAIT_TIMEOUT
+    assert int(torch.count_nonzero(out)) == 0
+    again = attention(q, tables, lens, T, 0)
+    torch.cuda.synchronize()
+    assert cache.status_bits() == 0
+    exact = attention_fp64(q[0].float().cpu().numpy(), *gather_oracle(keys, values, ks, vs, table, T, bs, 0))
+    assert_near_exact(again[0].float().cpu().numpy(), exact, "after a timed-out launch", scale=3.0)
