@@ -15,6 +15,19 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Streaming multiprocessors of the current device, queried once per device.
+inline int device_sms() {
+    static int counts[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (counts[dev] <= 0) {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+        counts[dev] = sms;
+    }
+    return counts[dev];
+}
+
 inline int dtype_size(int dtype) {
     switch (dtype) {
         case SDC_DTYPE_F32: return 4;

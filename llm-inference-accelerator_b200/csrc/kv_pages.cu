@@ -8,6 +8,7 @@
 // coalesced burst.  Vectors are enumerated with the head fastest, so
 // neighbouring groups read neighbouring source rows.
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <new>
@@ -303,53 +304,63 @@ __global__ void dequantize_vector_kernel(const int8_t* codes, int64_t count, dou
 struct RollbackArgs {
     Pool pool;
     const int64_t* slots;
-    uint32_t total_rows;  // cleared slots x layers: one warp each
-    uint32_t row_blocks;
-    uint32_t chunks;      // 16-byte code chunks of one slot and layer: 2 x heads x head_dim / 16
-    FastDiv div_layers;
+    uint32_t slot_blocks;  // cleared slots x layer spans: one block each
+    uint32_t span;         // layers one block clears
+    FastDiv div_spans;     // layer spans per slot
+    FastDiv div_chunks;    // 16-byte code chunks of one layer: 2 x heads x head_dim / 16
+    FastDiv div_vector;    // chunks of one head vector: head_dim / 16
+    FastDiv div_scales;    // scales of one layer: 2 x heads
     FastDiv div_block;
-    FastDiv div_chunks;   // chunks per head vector: head_dim / 16
     TableEdits edits;
     int32_t* status;
 };
 
-// One warp clears one (slot, layer): the key and value codes of every head,
-// 16-byte chunks spread over the lanes (a head vector's chunks are
-// contiguous, so eight lanes fill one 128-byte row at head_dim 128), and the
-// slot's 2 x heads scales.  The slot's address arithmetic is done once per
-// warp rather than once per chunk.
+// One block clears one cleared slot over a span of layers: the key and value
+// codes of every head, one 16-byte chunk per thread and step (consecutive
+// threads fill a head vector's contiguous row, so each warp store writes four
+// whole 128-byte rows at head_dim 128), then the span's 2 x heads scales per
+// layer.  The slot is read once per block and every store after it is
+// independent, so a block issues all of its writes back to back; the host
+// sizes the spans so that the grid covers every SM a few times over.
 __global__ void __launch_bounds__(256) rollback_kernel(RollbackArgs a) {
-    if (blockIdx.x >= a.row_blocks) {
+    if (blockIdx.x >= a.slot_blocks) {
         apply_table_edits(a.edits, threadIdx.x, blockDim.x, a.status);
         return;
     }
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (w >= a.total_rows) return;
-    uint32_t index, layer;
-    a.div_layers.divmod(w, index, layer);
+    uint32_t index, part;
+    a.div_spans.divmod(blockIdx.x, index, part);
     const int64_t slot = __ldg(a.slots + index);
     if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
-        if (lane == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
+        if (threadIdx.x == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
         return;
     }
     uint32_t blk, off;
     a.div_block.divmod(static_cast<uint32_t>(slot), blk, off);
+    const uint32_t L = static_cast<uint32_t>(a.pool.num_layers);
     const uint32_t H = static_cast<uint32_t>(a.pool.num_heads);
-    const int64_t code_off = blk * a.pool.cbs + layer * a.pool.cls + off * a.pool.head_dim;
-    for (uint32_t c = lane; c < a.chunks; c += 32) {
-        uint32_t row, ch;  // row: kv * H + head
-        a.div_chunks.divmod(c, row, ch);
+    const uint32_t l0 = part * a.span;
+    const uint32_t layers = L - l0 < a.span ? L - l0 : a.span;
+    const int64_t code_base = blk * a.pool.cbs + (int64_t)off * a.pool.head_dim;
+    const uint32_t chunks = layers * a.div_chunks.divisor;
+    for (uint32_t c = threadIdx.x; c < chunks; c += blockDim.x) {
+        uint32_t layer, rem, row, ch;
+        a.div_chunks.divmod(c, layer, rem);
+        a.div_vector.divmod(rem, row, ch);  // row: kv * H + head
         const bool value_side = row >= H;
         const uint32_t head = value_side ? row - H : row;
-        int8_t* codes = (value_side ? a.pool.values : a.pool.keys) + code_off + head * a.pool.chs + ch * 16;
+        int8_t* codes = (value_side ? a.pool.values : a.pool.keys) + code_base + (l0 + layer) * a.pool.cls +
+                        head * a.pool.chs + ch * 16;
         *reinterpret_cast<uint4*>(codes) = make_uint4(0u, 0u, 0u, 0u);
     }
-    const int64_t scale_off = blk * a.pool.sbs + layer * a.pool.sls + off;
-    for (uint32_t r = lane; r < 2 * H; r += 32) {
+    const int64_t scale_base = blk * a.pool.sbs + off;
+    const uint32_t scales = layers * a.div_scales.divisor;
+    for (uint32_t i = threadIdx.x; i < scales; i += blockDim.x) {
+        uint32_t layer, r;
+        a.div_scales.divmod(i, layer, r);
         const bool value_side = r >= H;
         const uint32_t head = value_side ? r - H : r;
-        (value_side ? a.pool.value_scales : a.pool.key_scales)[scale_off + head * a.pool.shs] = 0.0f;
+        (value_side ? a.pool.value_scales : a.pool.key_scales)[scale_base + (l0 + layer) * a.pool.sls +
+                                                              head * a.pool.shs] = 0.0f;
     }
 }
 
@@ -740,17 +751,26 @@ SDC_API sdc_status_t sdc_rollback(const sdc_page_pool_t* pool, const int64_t* cl
         RollbackArgs a;
         a.pool = to_pool(pool);
         a.slots = clear_slots;
-        const int64_t rows = num_clear * pool->num_layers;  // one warp per (slot, layer)
-        const int64_t nblocks = ceil_div(rows, kThreads / 32);
+        // layers per block: the whole slot when there are enough slots to
+        // cover every SM four times, otherwise spans small enough that they do
+        const int64_t L = pool->num_layers;
+        const int64_t want = 4 * static_cast<int64_t>(device_sms());
+        const int64_t splits = num_clear > 0 ? std::min<int64_t>(L, ceil_div(want, num_clear)) : 1;
+        const int64_t span = ceil_div(L, splits);
+        const int64_t spans = ceil_div(L, span);
+        const int64_t nblocks = num_clear * spans;
         const int64_t chunks = 2 * pool->num_heads * (pool->head_dim / 16);
-        if (rows >= INT32_MAX || nblocks + 1 >= INT32_MAX || chunks >= INT32_MAX) return SDC_STATUS_OVERFLOW;
+        if (nblocks + 1 >= INT32_MAX || chunks * span >= INT32_MAX || 2 * pool->num_heads * span >= INT32_MAX) {
+            return SDC_STATUS_OVERFLOW;
+        }
         if (pool->num_blocks * pool->block_size >= INT32_MAX) return SDC_STATUS_OVERFLOW;
-        a.total_rows = static_cast<uint32_t>(rows);
-        a.row_blocks = static_cast<uint32_t>(nblocks);
-        a.chunks = static_cast<uint32_t>(chunks);
-        a.div_layers = FastDiv(static_cast<uint32_t>(pool->num_layers));
+        a.slot_blocks = static_cast<uint32_t>(nblocks);
+        a.span = static_cast<uint32_t>(span);
+        a.div_spans = FastDiv(static_cast<uint32_t>(spans));
+        a.div_chunks = FastDiv(static_cast<uint32_t>(chunks));
+        a.div_vector = FastDiv(static_cast<uint32_t>(pool->head_dim / 16));
+        a.div_scales = FastDiv(static_cast<uint32_t>(2 * pool->num_heads));
         a.div_block = FastDiv(static_cast<uint32_t>(pool->block_size));
-        a.div_chunks = FastDiv(static_cast<uint32_t>(pool->head_dim / 16));
         a.edits = te;
         a.status = device_status;
         const int64_t blocks = nblocks + (has_edits ? 1 : 0);

@@ -16,6 +16,7 @@
 // run of words per thread and the lowest free ids found by a block-wide scan
 // of per-thread popcounts).  Page copies and slot zeroing run on a grid.
 
+#include <algorithm>
 #include <cub/block/block_reduce.cuh>
 #include <cub/block/block_scan.cuh>
 
@@ -265,6 +266,7 @@ struct TruncateArgs {
     int32_t sequences;
     int64_t max_removed;
     int32_t* status;
+    int64_t span;  // layers one zeroing block clears
 };
 
 __device__ __forceinline__ bool truncate_valid(const TruncateArgs& t, int s, int32_t* row, int64_t* old, int64_t* now) {
@@ -312,14 +314,17 @@ __global__ void __launch_bounds__(kPlanThreads) truncate_mark_kernel(TruncateArg
     }
 }
 
-// Block (touched page j, row s, layer) zeroes the rows to clear of that page
-// and layer -- every head, keys and values, codes and scales -- one 16-byte
-// chunk per thread.
+// Block (touched page j, row s, layer span z) zeroes the rows to clear of
+// that page in the span's layers -- every head, keys and values, codes and
+// scales -- one 16-byte chunk per thread and step.  The page's checks are
+// made once per block; the host sizes the spans so that the grid still
+// covers every SM a few times over.
 __global__ void __launch_bounds__(kCopyThreads) truncate_zero_kernel(TruncateArgs t) {
     const Alloc& a = t.a;
     const Pool& pool = t.pool;
     const int s = blockIdx.y;
-    const int64_t layer = blockIdx.z;
+    const int64_t layer0 = static_cast<int64_t>(blockIdx.z) * t.span;
+    const int layers = static_cast<int>(pool.num_layers - layer0 < t.span ? pool.num_layers - layer0 : t.span);
     int32_t row;
     int64_t old, now;
     if (!truncate_valid(t, s, &row, &old, &now) || now == old) return;
@@ -342,21 +347,26 @@ __global__ void __launch_bounds__(kCopyThreads) truncate_zero_kernel(TruncateArg
     const int H = static_cast<int>(pool.num_heads);
     const int row_chunks = static_cast<int>(pool.head_dim / 16);
     const int per_head = rows * row_chunks;
-    for (int c = threadIdx.x; c < 2 * H * per_head; c += blockDim.x) {
-        const int kvh = c / per_head, rem = c - kvh * per_head;
-        const int r = first + rem / row_chunks, ch = rem % row_chunks;
+    const int per_layer = 2 * H * per_head;
+    int8_t* const keys = pool.keys + blk * pool.cbs + layer0 * pool.cls + first * pool.head_dim;
+    int8_t* const values = pool.values + blk * pool.cbs + layer0 * pool.cls + first * pool.head_dim;
+    for (int c = threadIdx.x; c < layers * per_layer; c += blockDim.x) {
+        const int layer = c / per_layer, in_layer = c - layer * per_layer;
+        const int kvh = in_layer / per_head, rem = in_layer - kvh * per_head;
         const bool value_side = kvh >= H;
         const int head = value_side ? kvh - H : kvh;
-        int8_t* codes = (value_side ? pool.values : pool.keys) + blk * pool.cbs + layer * pool.cls +
-                        head * pool.chs + r * pool.head_dim + ch * 16;
+        // a head's rows to clear are contiguous: rem indexes their 16-byte chunks
+        int8_t* codes = (value_side ? values : keys) + layer * pool.cls + head * pool.chs + rem * 16;
         *reinterpret_cast<uint4*>(codes) = make_uint4(0u, 0u, 0u, 0u);
     }
-    for (int i = threadIdx.x; i < 2 * H * rows; i += blockDim.x) {
-        const int kvh = i / rows, r = first + i % rows;
+    const int scales_per_layer = 2 * H * rows;
+    for (int i = threadIdx.x; i < layers * scales_per_layer; i += blockDim.x) {
+        const int layer = i / scales_per_layer, in_layer = i - layer * scales_per_layer;
+        const int kvh = in_layer / rows, r = first + in_layer % rows;
         const bool value_side = kvh >= H;
         const int head = value_side ? kvh - H : kvh;
         float* scales = value_side ? pool.value_scales : pool.key_scales;
-        scales[blk * pool.sbs + layer * pool.sls + head * pool.shs + r] = 0.0f;
+        scales[blk * pool.sbs + (layer0 + layer) * pool.sls + head * pool.shs + r] = 0.0f;
     }
 }
 
@@ -507,16 +517,25 @@ SDC_API sdc_status_t sdc_pages_truncate(const sdc_page_allocator_t* allocator, c
         if (sequences < 1 || sequences > 65535 || max_removed < 0) return SDC_STATUS_INVALID_SIZE;
         if (max_removed > 65535) return SDC_STATUS_OVERFLOW;
         TruncateArgs t{a, to_pool(pool), rows, new_lengths, static_cast<int32_t>(sequences), max_removed,
-                       device_status};
+                       device_status, 1};
         cudaStream_t s = as_stream(stream);
         const unsigned row_blocks = static_cast<unsigned>(ceil_div(sequences, kPlanThreads));
         truncate_mark_kernel<<<row_blocks, kPlanThreads, 0, s>>>(t);
         if (max_removed > 0) {
             // pages a truncation of at most max_removed tokens touches
             const int64_t pages = (max_removed + a.block_size - 1) / a.block_size + 1;
-            if (pool->num_layers > 65535) return SDC_STATUS_UNSUPPORTED;
+            // layers per block: as many as keep the grid at four blocks per SM or more
+            const int64_t L = pool->num_layers;
+            const int64_t splits = std::min<int64_t>(L, ceil_div(4 * static_cast<int64_t>(device_sms()),
+                                                                 pages * sequences));
+            t.span = ceil_div(L, splits);
+            const int64_t spans = ceil_div(L, t.span);
+            if (spans > 65535 || pages > INT32_MAX) return SDC_STATUS_UNSUPPORTED;
+            if (t.span * 2 * pool->num_heads * a.block_size * (pool->head_dim / 16) >= INT32_MAX) {
+                return SDC_STATUS_OVERFLOW;
+            }
             truncate_zero_kernel<<<dim3(static_cast<unsigned>(pages), static_cast<unsigned>(sequences),
-                                        static_cast<unsigned>(pool->num_layers)),
+                                        static_cast<unsigned>(spans)),
                                    kCopyThreads, 0, s>>>(t);
         }
         truncate_finish_kernel<<<row_blocks, kPlanThreads, 0, s>>>(t);

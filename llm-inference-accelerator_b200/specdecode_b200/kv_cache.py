@@ -727,6 +727,39 @@ class PagedKVCache:
 
         return tuple(DequantizedKVToken(keys=nest(k[i]), values=nest(v[i])) for i in range(len(k)))
 
+    def gather_slots(self, slots, dtype, *, layer_begin: int = 0, layers: int | None = None, out=None):
+        """Dequantize the physical slots held in the device int64 tensor
+        ``slots`` (``block * block_size + offset`` per token, as
+        ``physical_slot`` gives): ``(keys, values)`` ``[n, layers, heads,
+        dim]`` in ``dtype``, written into ``out`` when given.  No host copy:
+        the slot list is already on the device (for example built from the
+        block tables by the caller)."""
+        torch = _torch()
+        layers = self.config.num_layers if layers is None else layers
+        if not isinstance(slots, torch.Tensor) or slots.dtype != torch.int64 or slots.dim() != 1:
+            raise TypeError("slots must be a 1-D int64 tensor")
+        if slots.device != torch.device(self.device):
+            raise ValueError("slots must be on the cache's device")
+        n = int(slots.numel())
+        shape = (n, layers, self.config.num_heads, self.config.head_dim)
+        if out is None:
+            out = (torch.empty(shape, dtype=dtype, device=self.device),
+                   torch.empty(shape, dtype=dtype, device=self.device))
+        out_k, out_v = out
+        if out_k.shape != shape or out_v.shape != shape or out_k.dtype != dtype or out_v.dtype != dtype:
+            raise ValueError("output tensors must be [n, layers, heads, dim] in the requested dtype")
+        if out_k.stride() != out_v.stride() or out_k.stride(3) != 1:
+            raise ValueError("output tensors must share strides with contiguous head vectors")
+        if n == 0:
+            return out_k, out_v
+        slots = slots.contiguous()
+        stream = self._stream()
+        self._lib.check(self._lib.handle.sdc_gather_dequantize(
+            self.pool_desc, layer_begin, layers, slots.data_ptr(), n, out_k.data_ptr(), out_v.data_ptr(),
+            _dtype_code(dtype), out_k.stride(0), out_k.stride(1), out_k.stride(2),
+            self._status.data_ptr(), stream.cuda_stream), "gather-dequantize")
+        return out_k, out_v
+
     def gather_sequence(self, sequence_id: Hashable, dtype, *, layer_begin: int = 0, layers: int | None = None):
         """Device tensors ``[T, layers, heads, dim]`` of dequantized K and V."""
         length = self.sequence_length(sequence_id)

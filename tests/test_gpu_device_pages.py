@@ -225,3 +225,43 @@ def test_faulted_calls_change_nothing(device):
     unchanged()
     with pytest.raises(ValueError):
         cache.reserve([0, 0], [1, 1])
+
+
+def test_truncate_zeroing_in_layer_spans_follows_the_reference(device):
+    """Enough rows and removed tokens that each zeroing block clears several
+    layers (nine layers in spans of three): the pool after every step equals
+    the reference allocator's, freed slots all zero."""
+    import torch
+
+    from oracle.paged_cache import PagedCacheOracle
+    from specdecode_b200.device_pages import DevicePagedCache
+    from specdecode_b200.kv_cache import KVCacheConfig
+
+    layers, nb, R = 9, 512, 64
+    rng = np.random.default_rng(17)
+    order = rng.permutation(nb)
+    cache = DevicePagedCache(KVCacheConfig(layers, H, D, block_size=BS, num_blocks=nb), max_rows=R,
+                             max_blocks_per_row=32, block_order=order, device=device)
+    oracle = PagedCacheOracle(layers, H, D, BS, nb, block_order=order, use_c=False)
+    rows = list(range(R))
+    for r in rows:
+        oracle.create_sequence(r)
+    for step in range(4):
+        keys = rng.standard_normal((R, 12, layers, H, D)).astype(np.float32)
+        values = rng.standard_normal((R, 12, layers, H, D)).astype(np.float32)
+        cache.append(rows, torch.from_numpy(keys), torch.from_numpy(values))
+        for i, r in enumerate(rows):
+            oracle.append_many(r, keys[i], values[i])
+        lengths = [max(0, oracle.sequence_length(r) - int(rng.integers(0, 13))) for r in rows]
+        cache.truncate(rows, lengths)
+        for r, n in zip(rows, lengths):
+            oracle.truncate(r, n)
+        cache.check_status()
+    cache.validate_invariants()
+    k = cache.key_codes.permute(0, 3, 1, 2, 4).contiguous().cpu().numpy()
+    v = cache.value_codes.permute(0, 3, 1, 2, 4).contiguous().cpu().numpy()
+    ks = cache.key_scale_pages.permute(0, 3, 1, 2).contiguous().cpu().numpy()
+    vs = cache.value_scale_pages.permute(0, 3, 1, 2).contiguous().cpu().numpy()
+    assert np.array_equal(k, oracle.keys) and np.array_equal(v, oracle.values)
+    assert np.array_equal(ks.view(np.uint32), oracle.key_scales.view(np.uint32))
+    assert np.array_equal(vs.view(np.uint32), oracle.value_scales.view(np.uint32))

@@ -232,3 +232,60 @@ def test_float64_entries_take_the_double_path(device):
     codes, scale = quantize_vector(vec)
     assert token.keys[0][0].values == codes and token.keys[0][0].scale == scale
     assert math.isfinite(token.values[0][0].scale)
+
+
+@pytest.mark.parametrize("layers,sequences,window", [(7, 64, 10), (32, 8, 5)])
+def test_rollback_spans_of_layers_match_oracle(device, layers, sequences, window):
+    """Rollbacks whose blocks clear several layers each (many rolled slots
+    over 7 layers: spans of 4 and a last span of 3; few slots over 32
+    layers: spans of 2): every released slot holds zeros, codes and scales,
+    and the kept ones are untouched."""
+    import torch
+
+    rng = np.random.default_rng(layers * 100 + sequences)
+    H, D, bs, nb = 2, 64, 16, 512
+    order = rng.permutation(nb)
+    cache = make_cache(device, layers, H, D, bs, nb, block_order=order, check_status=False)
+    oracle = PagedCacheOracle(layers, H, D, bs, nb, block_order=order)
+    seqs = list(range(sequences))
+    for s in seqs:
+        cache.create_sequence(s)
+        oracle.create_sequence(s)
+    for step in range(4):
+        k = torch.from_numpy(rng.standard_normal((sequences, window, layers, H, D))).to(torch.bfloat16)
+        v = torch.from_numpy(rng.standard_normal((sequences, window, layers, H, D))).to(torch.bfloat16)
+        cache.append_batch(seqs, k.to(device), v.to(device))
+        k64, v64 = k.double().numpy(), v.double().numpy()
+        for i, s in enumerate(seqs):
+            oracle.append_many(s, k64[i], v64[i])
+        rolled = rng.integers(0, window + 1, size=sequences)
+        counts = [cache.sequence_length(s) - int(r) for s, r in zip(seqs, rolled)]
+        assert cache.truncate_batch(seqs, counts) == [oracle.truncate(s, c) for s, c in zip(seqs, counts)]
+    assert cache.status_bits() == 0
+    keys, values, ks, vs = read_logical(cache)
+    assert np.array_equal(keys, oracle.keys)
+    assert np.array_equal(values, oracle.values)
+    assert np.array_equal(bits_f32(ks), bits_f32(oracle.key_scales))
+    assert np.array_equal(bits_f32(vs), bits_f32(oracle.value_scales))
+
+
+def test_gather_slots_equals_gather_sequence(device):
+    """The device-slot gather returns the same dequantized rows as the
+    sequence gather, for slots listed in any order."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    L, H, D, bs, nb = 2, 4, 128, 16, 64
+    cache = make_cache(device, L, H, D, bs, nb, block_order=rng.permutation(nb))
+    cache.create_sequence("a")
+    k = torch.from_numpy(rng.standard_normal((150, L, H, D))).to(torch.bfloat16).to(device)
+    v = torch.from_numpy(rng.standard_normal((150, L, H, D))).to(torch.bfloat16).to(device)
+    cache.append_tensor("a", k, v)
+    want_k, want_v = cache.gather_sequence("a", torch.float32)
+    slots = [b * bs + o for b, o in (cache.physical_slot("a", t) for t in range(150))]
+    perm = rng.permutation(150)
+    got_k, got_v = cache.gather_slots(torch.tensor([slots[i] for i in perm], device=device), torch.float32)
+    assert torch.equal(got_k, want_k[torch.from_numpy(perm).to(device)])
+    assert torch.equal(got_v, want_v[torch.from_numpy(perm).to(device)])
+    with pytest.raises(TypeError):
+        cache.gather_slots(torch.tensor(slots, dtype=torch.int32, device=device), torch.float32)
