@@ -416,10 +416,23 @@ __device__ int64_t row_search(const W& w, int64_t vocab, DD thr, RowShared& sh) 
                 const int src = __ffs(found) - 1;
                 const int64_t index = __shfl_sync(kFullMask, first + hit, src);
                 if (lane == 0) sh.index = index;
-            } else if (lane == 0) {
+            } else {
                 // The chunk-level sums passed the threshold but the per-weight
-                // running sum (added in another order) did not: the last weight.
-                sh.index = min(vocab - 1, chunk_first + kChunk - 1);
+                // running sum (added in another order) did not: the chunk's
+                // last index with a positive weight, where its running sum
+                // reaches the chunk's total (never a zero-weight or padding
+                // index).
+                int64_t last = -1;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    if (first + e < vocab && x[e] > 0.0) last = first + e;
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    const int64_t other = __shfl_xor_sync(kFullMask, last, off);
+                    last = other > last ? other : last;
+                }
+                if (lane == 0) sh.index = last >= 0 ? last : min(vocab - 1, chunk_first + kChunk - 1);
             }
         }
     }

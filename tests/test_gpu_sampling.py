@@ -147,6 +147,29 @@ def test_verify_batched_with_ragged_windows(device):
         assert within_ulps(probs[s, :n].cpu().numpy(), want.probabilities)
 
 
+def test_sample_never_lands_on_trailing_zero_weights(device):
+    """Rows whose positive weights end early in a long row (zeros after
+    them, across whole chunks of the kernel): a uniform just below 1 takes
+    the last positive weight, as the reference's running sum does, never a
+    zero-weight index after it."""
+    import torch
+
+    from specdecode_b200.sampling import sample_rows
+
+    vocab = 3000
+    rows = []
+    for last in (1, 127, 128, 129, 1000, 2047):
+        w = np.zeros(vocab)
+        w[: last + 1] = np.linspace(1.0, 2.0, last + 1)
+        rows.append(w)
+    weights = torch.tensor(np.array(rows), device=device)
+    uniforms = torch.full((len(rows),), 1.0 - 2.0 ** -53, dtype=torch.float64, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    got = sample_rows(weights, uniforms, status=status).cpu().tolist()
+    assert int(status.item()) == 0
+    assert got == [1, 127, 128, 129, 1000, 2047]
+
+
 def test_device_backend_known_answers(device):
     from specdecode_b200.sampling import DeviceSamplingBackend
 
