@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define SDC_ABI_VERSION UINT32_C(0x00020002)
+#define SDC_ABI_VERSION UINT32_C(0x00020003)
 
 /* Values 0-10 keep the meaning they have in the reference's sd_status_t
  * (native/include/specdecode/native.h:25-37). */
@@ -211,6 +211,46 @@ SDC_API sdc_status_t sdc_paged_verify_attention(
     int64_t batch, int64_t num_query_heads, int64_t window, const int32_t* block_tables,
     int64_t table_stride, const int32_t* context_lens, int64_t max_context_len, void* out,
     void* workspace, size_t workspace_bytes, int32_t* device_status, uintptr_t stream);
+
+/*
+ * sdc_paged_verify_attention for one rank of a KV-head split (the long-context
+ * configuration: rank r of `world` holds KV heads [r Hkv/world, (r+1)
+ * Hkv/world) of every page and the matching num_query_heads query heads),
+ * with the all-gather of the outputs fused into the attention's own output
+ * stores.  rank_outputs[i] (i < world) is rank i's gathered output
+ * [batch, world * num_query_heads, window, head_dim] in the query dtype,
+ * mapped into this process (sdc_peer_buffer_open for the other ranks');
+ * the kernel that writes this rank's output rows stores each row into every
+ * rank's buffer, at head offset rank * num_query_heads, over NVLink.
+ * rank_flags[i] is rank i's array of `world` uint32 flag words.  After the
+ * output launches, one more launch stores `epoch` into flag `rank` of every
+ * rank (release, system scope) and waits until this rank's flags all read
+ * `epoch` (acquire): when it ends, this rank's buffer holds every rank's rows.
+ * A wait that runs past about a second records SDC_FAULT_WAIT_TIMEOUT in
+ * device_status and ends.  `epoch` must differ from the previous call's (a
+ * per-call counter starting at 1; flag words start at 0).  Every rank must
+ * make the same calls in the same order.  No counterpart in the reference,
+ * which runs on one device; it replaces an all-gather collective after
+ * sdc_paged_verify_attention.
+ */
+SDC_API sdc_status_t sdc_paged_verify_attention_gather(
+    const sdc_page_pool_t* pool, int64_t layer, const void* query, int query_dtype,
+    int64_t batch, int64_t num_query_heads, int64_t window, const int32_t* block_tables,
+    int64_t table_stride, const int32_t* context_lens, int64_t max_context_len,
+    void* const* rank_outputs, uint32_t* const* rank_flags, int32_t world, int32_t rank,
+    uint32_t epoch, void* workspace, size_t workspace_bytes, int32_t* device_status,
+    uintptr_t stream);
+
+/* Device buffers other processes of the node can map (the gathered outputs
+ * and flag words of sdc_paged_verify_attention_gather): allocate (zeroed) on
+ * the current device, export an inter-process handle (SDC_PEER_HANDLE_BYTES
+ * bytes), map another process's buffer from its handle, unmap, free. */
+#define SDC_PEER_HANDLE_BYTES 64
+SDC_API sdc_status_t sdc_peer_buffer_alloc(size_t bytes, void** ptr);
+SDC_API sdc_status_t sdc_peer_buffer_free(void* ptr);
+SDC_API sdc_status_t sdc_peer_buffer_export(void* ptr, void* handle, size_t handle_bytes);
+SDC_API sdc_status_t sdc_peer_buffer_open(const void* handle, size_t handle_bytes, void** ptr);
+SDC_API sdc_status_t sdc_peer_buffer_close(void* ptr);
 
 /* Bytes of the library-owned scratch of sdc_paged_verify_attention_no_alloc. */
 #define SDC_NO_ALLOC_SCRATCH_BYTES ((size_t)16 << 20)

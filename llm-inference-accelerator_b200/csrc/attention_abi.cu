@@ -2,6 +2,7 @@
 // workspace layout, then the launch.
 
 #include <cmath>
+#include <cstring>
 
 #include "host_common.h"
 #include "paged_attention.h"
@@ -46,6 +47,119 @@ sdc_status_t make_plan(int64_t batch, int64_t hq, int64_t hkv, int64_t d, int64_
     return SDC_STATUS_OK;
 }
 
+// Where a call's output rows go (see AttnArgs).
+struct Outputs {
+    void* ptrs[kMaxOutputs] = {};
+    int32_t count = 0;
+    int64_t seq_stride = 0;
+    int64_t head0 = 0;
+};
+
+sdc_status_t run_attention(const sdc_page_pool_t* pool, int64_t layer, const void* query, int query_dtype,
+                           int64_t batch, int64_t num_query_heads, int64_t window, const int32_t* block_tables,
+                           int64_t table_stride, const int32_t* context_lens, int64_t max_context_len,
+                           const Outputs& o, void* workspace, size_t workspace_bytes, int32_t* device_status,
+                           cudaStream_t stream) {
+    sdc_status_t rc = validate_pool(pool);
+    if (rc != SDC_STATUS_OK) return rc;
+    if (query == nullptr || block_tables == nullptr || context_lens == nullptr || device_status == nullptr ||
+        workspace == nullptr) {
+        return SDC_STATUS_NULL_ARGUMENT;
+    }
+    if (layer < 0 || layer >= pool->num_layers) return SDC_STATUS_INVALID_SIZE;
+    if (table_stride < 1) return SDC_STATUS_INVALID_SIZE;
+    if (query_dtype != SDC_DTYPE_BF16 && query_dtype != SDC_DTYPE_F16 && query_dtype != SDC_DTYPE_F32) {
+        return SDC_STATUS_UNSUPPORTED;
+    }
+    if (!aligned16(query) || !aligned16(workspace)) return SDC_STATUS_MISALIGNED;
+    for (int i = 0; i < o.count; ++i) {
+        if (!aligned16(o.ptrs[i])) return SDC_STATUS_MISALIGNED;
+    }
+    Plan p;
+    rc = make_plan(batch, num_query_heads, pool->num_heads, pool->head_dim, window, max_context_len, &p);
+    if (rc != SDC_STATUS_OK) return rc;
+    if (workspace_bytes < p.total) return SDC_STATUS_INVALID_SIZE;
+    if (p.max_chunks > 65535 || batch * pool->num_heads > 65535) return SDC_STATUS_UNSUPPORTED;
+
+    AttnArgs a;
+    a.pool = to_pool(pool);
+    a.layer = layer;
+    a.query = query;
+    a.query_dtype = query_dtype;
+    for (int i = 0; i < kMaxOutputs; ++i) a.outs[i] = i < o.count ? o.ptrs[i] : nullptr;
+    a.num_outs = o.count;
+    a.out_seq_stride = o.seq_stride;
+    a.out_head0 = o.head0;
+    a.batch = batch;
+    a.query_heads = num_query_heads;
+    a.kv_heads = pool->num_heads;
+    a.group = num_query_heads / pool->num_heads;
+    a.window = window;
+    a.rows = p.rows;
+    a.head_dim = pool->head_dim;
+    a.block_tables = block_tables;
+    a.table_stride = table_stride;
+    a.context_lens = context_lens;
+    a.chunk = p.chunk;
+    a.max_chunks = p.max_chunks;
+    a.part_o = static_cast<float*>(workspace);
+    a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.part_o_bytes);
+    a.status = device_status;
+    a.qk_scale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(pool->head_dim)));
+    if (p.tensor_cores && tc::supports(a)) {
+        void* extra = static_cast<char*>(workspace) + p.part_o_bytes + p.part_ml_bytes;
+        return tc::launch(a, extra, stream);
+    }
+    return launch_attention_simt(a, stream);
+}
+
+// Completion of the KV-head all-gather: thread p < world stores `epoch` into
+// rank p's flag word for this rank (a release at system scope, after the
+// output launches' stores, which each made visible system-wide), then waits
+// for its own flag word of rank p to read `epoch` (acquire).  A wait gives up
+// after a bounded number of cycles and records SDC_FAULT_WAIT_TIMEOUT.
+struct SignalArgs {
+    uint32_t* flags[kMaxOutputs];
+    int32_t world;
+    int32_t rank;
+    uint32_t epoch;
+    long long wait_limit;
+    int32_t* status;
+};
+
+__global__ void __launch_bounds__(32) gather_signal_kernel(SignalArgs s) {
+    const int p = threadIdx.x;
+    if (p >= s.world) return;
+    __threadfence_system();
+    uint32_t* to = s.flags[p] + s.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(to), "r"(s.epoch) : "memory");
+    const uint32_t* mine = s.flags[s.rank] + p;
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if (v == s.epoch) break;
+        if (clock64() - t0 > s.wait_limit) {
+            atomicOr(s.status, SDC_FAULT_WAIT_TIMEOUT);
+            break;
+        }
+        __nanosleep(64);
+    }
+}
+
+sdc_status_t launch_gather_signal(uint32_t* const* flags, int32_t world, int32_t rank, uint32_t epoch,
+                                  int32_t* status, cudaStream_t stream) {
+    SignalArgs s;
+    for (int i = 0; i < kMaxOutputs; ++i) s.flags[i] = i < world ? flags[i] : nullptr;
+    s.world = world;
+    s.rank = rank;
+    s.epoch = epoch;
+    s.wait_limit = tc::wait_limit_cycles();
+    s.status = status;
+    gather_signal_kernel<<<1, 32, 0, stream>>>(s);
+    return launch_status();
+}
+
 }  // namespace
 }  // namespace sdc
 
@@ -76,54 +190,110 @@ SDC_API sdc_status_t sdc_paged_verify_attention(const sdc_page_pool_t* pool, int
                                                 void* workspace, size_t workspace_bytes, int32_t* device_status,
                                                 uintptr_t stream) {
     try {
-        sdc_status_t rc = validate_pool(pool);
-        if (rc != SDC_STATUS_OK) return rc;
-        if (query == nullptr || out == nullptr || block_tables == nullptr || context_lens == nullptr ||
-            device_status == nullptr || workspace == nullptr) {
-            return SDC_STATUS_NULL_ARGUMENT;
-        }
-        if (layer < 0 || layer >= pool->num_layers) return SDC_STATUS_INVALID_SIZE;
-        if (table_stride < 1) return SDC_STATUS_INVALID_SIZE;
-        if (query_dtype != SDC_DTYPE_BF16 && query_dtype != SDC_DTYPE_F16 && query_dtype != SDC_DTYPE_F32) {
-            return SDC_STATUS_UNSUPPORTED;
-        }
-        if (!aligned16(query) || !aligned16(out) || !aligned16(workspace)) return SDC_STATUS_MISALIGNED;
-        Plan p;
-        rc = make_plan(batch, num_query_heads, pool->num_heads, pool->head_dim, window, max_context_len, &p);
-        if (rc != SDC_STATUS_OK) return rc;
-        if (workspace_bytes < p.total) return SDC_STATUS_INVALID_SIZE;
-        if (p.max_chunks > 65535 || batch * pool->num_heads > 65535) return SDC_STATUS_UNSUPPORTED;
-
-        AttnArgs a;
-        a.pool = to_pool(pool);
-        a.layer = layer;
-        a.query = query;
-        a.query_dtype = query_dtype;
-        a.out = out;
-        a.batch = batch;
-        a.query_heads = num_query_heads;
-        a.kv_heads = pool->num_heads;
-        a.group = num_query_heads / pool->num_heads;
-        a.window = window;
-        a.rows = p.rows;
-        a.head_dim = pool->head_dim;
-        a.block_tables = block_tables;
-        a.table_stride = table_stride;
-        a.context_lens = context_lens;
-        a.chunk = p.chunk;
-        a.max_chunks = p.max_chunks;
-        a.part_o = static_cast<float*>(workspace);
-        a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.part_o_bytes);
-        a.status = device_status;
-        a.qk_scale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(pool->head_dim)));
-        if (p.tensor_cores && tc::supports(a)) {
-            void* extra = static_cast<char*>(workspace) + p.part_o_bytes + p.part_ml_bytes;
-            return tc::launch(a, extra, as_stream(stream));
-        }
-        return launch_attention_simt(a, as_stream(stream));
+        if (out == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        Outputs o;
+        o.ptrs[0] = out;
+        o.count = 1;
+        o.seq_stride = num_query_heads * window * (pool != nullptr ? pool->head_dim : 0);
+        o.head0 = 0;
+        return run_attention(pool, layer, query, query_dtype, batch, num_query_heads, window, block_tables,
+                             table_stride, context_lens, max_context_len, o, workspace, workspace_bytes,
+                             device_status, as_stream(stream));
     } catch (...) {
         return SDC_STATUS_INTERNAL_ERROR;
     }
+}
+
+SDC_API sdc_status_t sdc_paged_verify_attention_gather(
+    const sdc_page_pool_t* pool, int64_t layer, const void* query, int query_dtype, int64_t batch,
+    int64_t num_query_heads, int64_t window, const int32_t* block_tables, int64_t table_stride,
+    const int32_t* context_lens, int64_t max_context_len, void* const* rank_outputs, uint32_t* const* rank_flags,
+    int32_t world, int32_t rank, uint32_t epoch, void* workspace, size_t workspace_bytes, int32_t* device_status,
+    uintptr_t stream) {
+    try {
+        if (rank_outputs == nullptr || rank_flags == nullptr || device_status == nullptr) {
+            return SDC_STATUS_NULL_ARGUMENT;
+        }
+        if (world < 1 || world > kMaxOutputs || rank < 0 || rank >= world || epoch == 0) {
+            return SDC_STATUS_INVALID_ARGUMENT;
+        }
+        Outputs o;
+        for (int i = 0; i < world; ++i) {
+            if (rank_outputs[i] == nullptr || rank_flags[i] == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+            if (!aligned16(rank_outputs[i]) || (reinterpret_cast<uintptr_t>(rank_flags[i]) & 3u)) {
+                return SDC_STATUS_MISALIGNED;
+            }
+            o.ptrs[i] = rank_outputs[i];
+        }
+        o.count = world;
+        o.seq_stride = static_cast<int64_t>(world) * num_query_heads * window * (pool != nullptr ? pool->head_dim : 0);
+        o.head0 = static_cast<int64_t>(rank) * num_query_heads;
+        cudaStream_t st = as_stream(stream);
+        const sdc_status_t rc = run_attention(pool, layer, query, query_dtype, batch, num_query_heads, window,
+                                              block_tables, table_stride, context_lens, max_context_len, o,
+                                              workspace, workspace_bytes, device_status, st);
+        if (rc != SDC_STATUS_OK) return rc;
+        return launch_gather_signal(rank_flags, world, rank, epoch, device_status, st);
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_peer_buffer_alloc(size_t bytes, void** ptr) {
+    try {
+        if (ptr == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        *ptr = nullptr;
+        if (bytes == 0) return SDC_STATUS_INVALID_SIZE;
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
+        if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+            cudaFree(p);
+            return SDC_STATUS_CUDA_ERROR;
+        }
+        *ptr = p;
+        return SDC_STATUS_OK;
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_peer_buffer_free(void* ptr) {
+    if (ptr == nullptr) return SDC_STATUS_OK;
+    return cudaFree(ptr) == cudaSuccess ? SDC_STATUS_OK : SDC_STATUS_CUDA_ERROR;
+}
+
+SDC_API sdc_status_t sdc_peer_buffer_export(void* ptr, void* handle, size_t handle_bytes) {
+    try {
+        if (ptr == nullptr || handle == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        if (handle_bytes < sizeof(cudaIpcMemHandle_t)) return SDC_STATUS_INVALID_SIZE;
+        cudaIpcMemHandle_t h;
+        if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
+        std::memcpy(handle, &h, sizeof(h));
+        return SDC_STATUS_OK;
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_peer_buffer_open(const void* handle, size_t handle_bytes, void** ptr) {
+    try {
+        if (handle == nullptr || ptr == nullptr) return SDC_STATUS_NULL_ARGUMENT;
+        *ptr = nullptr;
+        if (handle_bytes < sizeof(cudaIpcMemHandle_t)) return SDC_STATUS_INVALID_SIZE;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handle, sizeof(h));
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
+        *ptr = p;
+        return SDC_STATUS_OK;
+    } catch (...) {
+        return SDC_STATUS_INTERNAL_ERROR;
+    }
+}
+
+SDC_API sdc_status_t sdc_peer_buffer_close(void* ptr) {
+    if (ptr == nullptr) return SDC_STATUS_OK;
+    return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? SDC_STATUS_OK : SDC_STATUS_CUDA_ERROR;
 }
 
 }  // extern "C"

@@ -253,14 +253,36 @@ __global__ void __launch_bounds__(kThreadsAttn) attn_simt_kernel(AttnArgs a) {
     }
 }
 
+// Four consecutive output elements in one store (8 bytes for 16-bit types,
+// 16 for float); the element offset is a multiple of 4.
 template <typename QT>
-__device__ __forceinline__ QT from_float(float v);
+__device__ __forceinline__ void store4(QT* dst, float x, float y, float z, float w);
 template <>
-__device__ __forceinline__ float from_float<float>(float v) { return v; }
+__device__ __forceinline__ void store4<float>(float* dst, float x, float y, float z, float w) {
+    *reinterpret_cast<float4*>(dst) = make_float4(x, y, z, w);
+}
 template <>
-__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* dst, float x, float y, float z, float w) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(x, y), hi = __floats2bfloat162_rn(z, w);
+    *reinterpret_cast<uint2*>(dst) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
 template <>
-__device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
+__device__ __forceinline__ void store4<__half>(__half* dst, float x, float y, float z, float w) {
+    const __half2 lo = __floats2half2_rn(x, y), hi = __floats2half2_rn(z, w);
+    *reinterpret_cast<uint2*>(dst) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+// The four elements at `offset` of every destination of the call (one, or
+// every rank's gathered output).  Stores that reach another GPU's memory are
+// made visible system-wide before the thread moves on to the completion
+// signal, which the launch after this one raises.
+template <typename QT>
+__device__ __forceinline__ void put4(const AttnArgs& a, int64_t offset, float x, float y, float z, float w) {
+    for (int i = 0; i < a.num_outs; ++i) store4<QT>(static_cast<QT*>(a.outs[i]) + offset, x, y, z, w);
+    if (a.num_outs > 1) __threadfence_system();
+}
 
 // Merges the chunk partials of one (sequence, KV head) and a group of its
 // query rows and writes the output.  D / 4 threads cover a row (4 columns
@@ -287,16 +309,13 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(AttnArgs 
     const int nr = min(rpb, R - r0);
     if (nr <= 0) return;
     const int64_t T = __ldg(a.context_lens + b);
-    QT* out = static_cast<QT*>(a.out) + ((b * a.query_heads + h * a.group) * a.window) * D;
+    const int64_t out = out_rows_offset(a, b, h);
     const bool valid_ctx = T >= a.window && T <= a.table_stride * a.pool.block_size &&
                            T <= a.max_chunks * a.chunk;
     const int rl = threadIdx.x / per_row;  // this thread's row within the group
     const int d4 = (threadIdx.x % per_row) * 4;
     if (!valid_ctx) {
-        if (rl < nr) {
-            QT* dst = out + (r0 + rl) * D + d4;
-            for (int e = 0; e < 4; ++e) dst[e] = from_float<QT>(0.0f);
-        }
+        if (rl < nr) put4<QT>(a, out + (r0 + rl) * D + d4, 0.0f, 0.0f, 0.0f, 0.0f);
         return;
     }
     const int chunks = static_cast<int>((T + a.chunk - 1) / a.chunk);
@@ -335,11 +354,7 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(AttnArgs 
         o.z = fmaf(v.z, w, o.z);
         o.w = fmaf(v.w, w, o.w);
     }
-    QT* dst = out + r * D + d4;
-    dst[0] = from_float<QT>(o.x);
-    dst[1] = from_float<QT>(o.y);
-    dst[2] = from_float<QT>(o.z);
-    dst[3] = from_float<QT>(o.w);
+    put4<QT>(a, out + r * D + d4, o.x, o.y, o.z, o.w);
 }
 
 template <typename QT, int D>

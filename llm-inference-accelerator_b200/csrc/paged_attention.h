@@ -8,12 +8,22 @@
 
 namespace sdc {
 
+// Destinations one call may write its output rows to: the caller's buffer,
+// or, with the KV-head all-gather, every rank's gathered output.
+constexpr int kMaxOutputs = 8;
+
 struct AttnArgs {
     Pool pool;
     int64_t layer;
     const void* query;
     int query_dtype;
-    void* out;
+    // Element (b, query head h, window row w, d) of this call goes to
+    // outs[i] + b * out_seq_stride + ((out_head0 + h) * window + w) * head_dim + d
+    // in every destination i < num_outs.
+    void* outs[kMaxOutputs];
+    int32_t num_outs;
+    int64_t out_seq_stride;  // elements between sequences of a destination
+    int64_t out_head0;       // first query head of this call in a destination
     int64_t batch;
     int64_t query_heads;
     int64_t kv_heads;
@@ -31,6 +41,12 @@ struct AttnArgs {
     int32_t* status;
     float qk_scale;      // log2(e) / sqrt(head_dim)
 };
+
+// Element offset, in every destination, of the first output row of KV head
+// h of sequence b (its group x window rows follow contiguously).
+__host__ __device__ __forceinline__ int64_t out_rows_offset(const AttnArgs& a, int64_t b, int64_t h) {
+    return b * a.out_seq_stride + (a.out_head0 + h * a.group) * a.window * a.head_dim;
+}
 
 bool simt_supports(int64_t head_dim, int64_t rows);
 sdc_status_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream);
@@ -50,6 +66,9 @@ bool supports(const AttnArgs& a);
 int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len, int64_t rows);
 size_t extra_workspace(int64_t batch, int64_t kv_heads, int64_t max_chunks, int64_t rows);
 sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t stream);
+// Cycles a bounded wait may take before it gives up (about a second unless
+// sdc_test_attention_waits set a shorter limit).
+long long wait_limit_cycles();
 }  // namespace tc
 
 }  // namespace sdc

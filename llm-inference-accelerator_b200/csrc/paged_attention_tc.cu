@@ -386,14 +386,16 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t w0, uint32_t w1, uin
     return __byte_perm(__byte_perm(w0, w1, 0x0040), __byte_perm(w2, w3, 0x0040), 0x5410);
 }
 
-// One output element in the query's dtype.
+// One output element in the query's dtype, in every destination of the call.
 __device__ __forceinline__ void store_output(const AttnArgs& a, int64_t index, float v) {
-    if (a.query_dtype == SDC_DTYPE_BF16) {
-        static_cast<__nv_bfloat16*>(a.out)[index] = __float2bfloat16_rn(v);
-    } else if (a.query_dtype == SDC_DTYPE_F16) {
-        static_cast<__half*>(a.out)[index] = __float2half_rn(v);
-    } else {
-        static_cast<float*>(a.out)[index] = v;
+    for (int i = 0; i < a.num_outs; ++i) {
+        if (a.query_dtype == SDC_DTYPE_BF16) {
+            static_cast<__nv_bfloat16*>(a.outs[i])[index] = __float2bfloat16_rn(v);
+        } else if (a.query_dtype == SDC_DTYPE_F16) {
+            static_cast<__half*>(a.outs[i])[index] = __float2half_rn(v);
+        } else {
+            static_cast<float*>(a.outs[i])[index] = v;
+        }
     }
 }
 
@@ -1079,14 +1081,42 @@ __global__ void __launch_bounds__(Roles<G>::kThreads, 1)
                 if (!merged) break;
                 if (t.direct) {
                     // every item covers its sequence's whole context: it writes
-                    // the normalised output rows itself (no partial, no combine)
+                    // the normalised output rows itself (no partial, no combine);
+                    // the row factors are gathered first so the stores issue
+                    // back to back, and the dtype is branched on once
                     const float inv_lane = l_lane > 0.0f ? 1.0f / l_lane : 0.0f;
-                    const int64_t q0 = (static_cast<int64_t>(it.b) * a.query_heads + it.h * a.group) * a.window + row0;
+                    float v[RB];
 #pragma unroll
                     for (int r = 0; r < RB; ++r) {
-                        const float inv = __shfl_sync(kFullMask, inv_lane, r);
-                        const float o0 = (r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x;
-                        if (r < R && o_row) store_output(a, (q0 + r) * HD + dcol, o0 * inv);
+                        v[r] = ((r & 1) ? o_acc[r / 2].y : o_acc[r / 2].x) * __shfl_sync(kFullMask, inv_lane, r);
+                    }
+                    if (o_row) {
+                        // every destination: the caller's buffer, or each rank's
+                        // gathered output (stores to another GPU made visible
+                        // system-wide before the completion signal)
+                        const int64_t e0 = out_rows_offset(a, it.b, it.h) + row0 * HD + dcol;
+                        for (int i = 0; i < a.num_outs; ++i) {
+                            if (a.query_dtype == SDC_DTYPE_BF16) {
+                                __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.outs[i]) + e0;
+#pragma unroll
+                                for (int r = 0; r < RB; ++r) {
+                                    if (r < R) out[r * HD] = __float2bfloat16_rn(v[r]);
+                                }
+                            } else if (a.query_dtype == SDC_DTYPE_F16) {
+                                __half* out = static_cast<__half*>(a.outs[i]) + e0;
+#pragma unroll
+                                for (int r = 0; r < RB; ++r) {
+                                    if (r < R) out[r * HD] = __float2half_rn(v[r]);
+                                }
+                            } else {
+                                float* out = static_cast<float*>(a.outs[i]) + e0;
+#pragma unroll
+                                for (int r = 0; r < RB; ++r) {
+                                    if (r < R) out[r * HD] = v[r];
+                                }
+                            }
+                        }
+                        if (a.num_outs > 1) __threadfence_system();
                     }
                 } else {
                     const int64_t bh = static_cast<int64_t>(it.b) * a.kv_heads + it.h;
@@ -1172,8 +1202,9 @@ __global__ void __launch_bounds__(256) prep_kernel(TcArgs t, int32_t* first) {
             const int64_t T = __ldg(a.context_lens + b);
             const bool valid = T >= a.window && T <= a.table_stride * a.pool.block_size && T <= a.max_chunks * a.chunk;
             if (!valid && has_d && r < t.rows && row < t.total_rows) {
-                const int64_t e0 = ((b * a.query_heads + h * a.group) * a.window + row) * HD + d;
+                const int64_t e0 = out_rows_offset(a, b, h) + row * HD + d;
                 for (int i = 0; i < 4; ++i) store_output(a, e0 + i, 0.0f);
+                if (a.num_outs > 1) __threadfence_system();
             }
         }
         float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -1385,16 +1416,7 @@ int64_t split_rows(int64_t rows) {
     return sp > 0 ? (rows + sp - 1) / sp : 0;
 }
 
-int num_sms() {
-    static int sms = 0;
-    if (sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
-    }
-    return sms;
-}
+int num_sms() { return device_sms(); }
 
 // Test hooks of the pipeline waits (sdc_test_attention_waits): the limit in
 // cycles and the stall flag that the next launches carry.
@@ -1528,6 +1550,8 @@ sdc_status_t launch(const AttnArgs& a, void* extra, cudaStream_t st) {
     if (t.direct) return SDC_STATUS_OK;  // every item wrote its output rows
     return launch_attention_combine(a, st, /*programmatic=*/true);
 }
+
+long long wait_limit_cycles() { return g_wait_limit.load(std::memory_order_relaxed); }
 
 }  // namespace tc
 }  // namespace sdc

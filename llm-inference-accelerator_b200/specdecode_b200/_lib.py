@@ -15,7 +15,8 @@ import os
 import threading
 from pathlib import Path
 
-ABI_VERSION = 0x00020002
+ABI_VERSION = 0x00020003
+PEER_HANDLE_BYTES = 64  # SDC_PEER_HANDLE_BYTES
 LIBRARY_NAME = "libspecdecode_cuda.so"
 _ENV = "SPECDECODE_CUDA_LIBRARY"
 
@@ -95,6 +96,12 @@ EXPORTED_SYMBOLS = (
     "sdc_paged_verify_attention",
     "sdc_gather_dequantize",
     "sdc_paged_verify_attention_no_alloc",
+    "sdc_paged_verify_attention_gather",
+    "sdc_peer_buffer_alloc",
+    "sdc_peer_buffer_free",
+    "sdc_peer_buffer_export",
+    "sdc_peer_buffer_open",
+    "sdc_peer_buffer_close",
     "sdc_test_attention_waits",
     "sdc_normalize_rows",
     "sdc_sample_categorical_rows",
@@ -260,6 +267,21 @@ class CudaLibrary:
         h.sdc_paged_verify_attention_no_alloc.argtypes = [
             ctypes.POINTER(PagePool), i64, vp, ctypes.c_int, i64, i64, i64, vp, i64, vp, i64, vp, vp, u]
         h.sdc_paged_verify_attention_no_alloc.restype = ctypes.c_int
+        h.sdc_paged_verify_attention_gather.argtypes = [
+            ctypes.POINTER(PagePool), i64, vp, ctypes.c_int, i64, i64, i64, vp, i64, vp, i64,
+            ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, vp,
+            ctypes.c_size_t, vp, u]
+        h.sdc_paged_verify_attention_gather.restype = ctypes.c_int
+        h.sdc_peer_buffer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+        h.sdc_peer_buffer_alloc.restype = ctypes.c_int
+        h.sdc_peer_buffer_free.argtypes = [vp]
+        h.sdc_peer_buffer_free.restype = ctypes.c_int
+        h.sdc_peer_buffer_export.argtypes = [vp, vp, ctypes.c_size_t]
+        h.sdc_peer_buffer_export.restype = ctypes.c_int
+        h.sdc_peer_buffer_open.argtypes = [vp, ctypes.c_size_t, ctypes.POINTER(vp)]
+        h.sdc_peer_buffer_open.restype = ctypes.c_int
+        h.sdc_peer_buffer_close.argtypes = [vp]
+        h.sdc_peer_buffer_close.restype = ctypes.c_int
         h.sdc_test_attention_waits.argtypes = [i64, ctypes.c_int32]
         h.sdc_test_attention_waits.restype = ctypes.c_int
         h.sdc_gather_dequantize.argtypes = [

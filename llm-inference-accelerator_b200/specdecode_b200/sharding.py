@@ -126,3 +126,153 @@ class TensorParallelVerifyAttention:
     def __call__(self, query, block_tables, context_lens, max_context_len: int, layer: int):
         out = self.local(query, block_tables, context_lens, max_context_len, layer)
         return gather_heads(out, self.shard, self.group)
+
+
+class _DeviceWords:
+    """A device allocation seen as a 1-D tensor of 16-bit words (``torch.as_tensor``
+    reads ``__cuda_array_interface__``; the caller views it as bf16 / fp16)."""
+
+    def __init__(self, pointer: int, words: int) -> None:
+        self.__cuda_array_interface__ = {"shape": (words,), "typestr": "<i2", "data": (pointer, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerHeadGather:
+    """KV-head tensor-parallel verify attention whose all-gather is fused into
+    the attention launch (``sdc_paged_verify_attention_gather``).
+
+    Every rank owns one device buffer holding its gathered output ``[batch,
+    query_heads, window, head_dim]`` and one flag word per rank.  The buffers
+    are mapped into every rank's process once (inter-process handles
+    exchanged over ``group``, the only use of torch.distributed here).  On a
+    call, the kernel that writes this rank's output rows stores each row into
+    every rank's buffer over NVLink; one more launch then raises this rank's
+    flag in every buffer and waits (bounded) until every rank's flag in its
+    own buffer carries the call's epoch.  When ``__call__`` returns, the
+    returned tensor -- a view of this rank's buffer, valid until ``close`` --
+    holds every rank's heads once the stream reaches that point.  No
+    collective runs on the data path and no library kernel touches another
+    GPU's memory.
+
+    ``cache`` is this rank's head-shard pool (``shard.kv_per_rank`` KV
+    heads); every rank must call with the same batch shape, in the same
+    order.
+    """
+
+    def __init__(self, cache, shard: HeadShard, batch: int, window: int, *, dtype=None, group=None) -> None:
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from specdecode_b200 import _lib
+
+        if shard.world > 8:
+            raise ValueError("the fused head gather serves at most 8 ranks")
+        if cache.config.num_heads != shard.kv_per_rank:
+            raise ValueError("the cache must hold this rank's KV heads only")
+        self.cache = cache
+        self.shard = shard
+        self.batch = int(batch)
+        self.window = int(window)
+        self.dtype = torch.bfloat16 if dtype is None else dtype
+        if self.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("the gathered output is bf16 or fp16")
+        self.group = group
+        self.library = cache.library
+        lib = self.library.handle
+        D = cache.config.head_dim
+        self.shape = (self.batch, shard.query_heads, self.window, D)
+        elements = self.batch * shard.query_heads * self.window * D
+        self._out_bytes = -(-elements * 2 // 256) * 256
+        total = self._out_bytes + 256
+        own = ctypes.c_void_p()
+        self.library.check(lib.sdc_peer_buffer_alloc(total, ctypes.byref(own)), "peer buffer allocation")
+        self._own = int(own.value)
+        self._opened: list[int] = []
+        try:
+            handle = (ctypes.c_char * _lib.PEER_HANDLE_BYTES)()
+            self.library.check(lib.sdc_peer_buffer_export(self._own, handle, len(handle)), "peer buffer export")
+            handles: list = [None] * shard.world
+            if shard.world > 1:
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            else:
+                handles = [bytes(handle)]
+            bases = []
+            for r, h in enumerate(handles):
+                if r == shard.rank:
+                    bases.append(self._own)
+                    continue
+                ptr = ctypes.c_void_p()
+                raw = (ctypes.c_char * len(h)).from_buffer_copy(h)
+                self.library.check(lib.sdc_peer_buffer_open(raw, len(h), ctypes.byref(ptr)), "peer buffer open")
+                self._opened.append(int(ptr.value))
+                bases.append(int(ptr.value))
+        except BaseException:
+            self._release_maps()
+            raise
+        self._outs = (ctypes.c_void_p * shard.world)(*bases)
+        self._flags = (ctypes.c_void_p * shard.world)(*[b + self._out_bytes for b in bases])
+        words = torch.as_tensor(_DeviceWords(self._own, elements), device=cache.device)
+        self.output = words.view(self.dtype).view(self.shape)
+        self._attention_sizes: dict[int, int] = {}
+        self._workspace = None
+        self.epoch = 0
+
+    def _release_maps(self) -> None:
+        lib = self.library.handle
+        for ptr in self._opened:
+            lib.sdc_peer_buffer_close(ptr)
+        self._opened = []
+        if self._own:
+            lib.sdc_peer_buffer_free(self._own)
+            self._own = 0
+
+    def __call__(self, query, block_tables, context_lens, max_context_len: int, layer: int):
+        import ctypes
+
+        import torch
+
+        from specdecode_b200.kv_cache import _dtype_code
+
+        if self._own == 0:
+            raise RuntimeError("the head gather is closed")
+        if tuple(query.shape) != self.shape or query.dtype != self.dtype:
+            raise ValueError(f"query must be {self.shape} in {self.dtype}")
+        q = shard_query(query, self.shard).contiguous()
+        B, hq, kw, _ = (int(d) for d in q.shape)
+        if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
+            raise ValueError("block tables and context lengths must be int32")
+        block_tables = block_tables.contiguous()
+        lib = self.library.handle
+        need = self._attention_sizes.get(int(max_context_len))
+        if need is None:
+            size = ctypes.c_size_t()
+            self.library.check(lib.sdc_paged_attention_workspace_size(
+                B, hq, self.cache.config.num_heads, self.cache.config.head_dim, kw, int(max_context_len),
+                ctypes.byref(size)), "attention workspace sizing")
+            need = self._attention_sizes[int(max_context_len)] = int(size.value)
+        if self._workspace is None or self._workspace.numel() < need:
+            self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=self.cache.device)
+        self.epoch = self.epoch % 0xFFFFFFFF + 1
+        stream = torch.cuda.current_stream(self.cache.device)
+        self.library.check(lib.sdc_paged_verify_attention_gather(
+            self.cache.pool_desc, int(layer), q.data_ptr(), _dtype_code(q.dtype), B, hq, kw,
+            block_tables.data_ptr(), block_tables.stride(0), context_lens.data_ptr(), int(max_context_len),
+            self._outs, self._flags, self.shard.world, self.shard.rank, self.epoch, self._workspace.data_ptr(),
+            self._workspace.numel(), self.cache._status.data_ptr(), stream.cuda_stream), "fused head gather")
+        return self.output
+
+    def close(self) -> None:
+        """Unmaps the other ranks' buffers and frees this rank's, after every
+        rank has finished its calls (a barrier over ``group``)."""
+        import torch
+        import torch.distributed as dist
+
+        if self._own == 0:
+            return
+        torch.cuda.synchronize(self.cache.device)
+        if self.shard.world > 1:
+            dist.barrier(group=self.group)
+        self.output = None
+        self._release_maps()

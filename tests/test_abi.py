@@ -43,7 +43,7 @@ def test_no_undeclared_sdc_symbols_are_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.handle.sdc_abi_version() == _lib.ABI_VERSION == 0x00020002
+    assert lib.handle.sdc_abi_version() == _lib.ABI_VERSION == 0x00020003
     assert lib.status_string(0) == "ok"
     assert lib.status_string(3) == "non-finite value"
     assert lib.status_string(10) == "invalid quantization scale"
@@ -135,3 +135,40 @@ def test_page_allocator_entry_points_validate_on_the_host(lib):
     assert h.sdc_pages_fork(ctypes.byref(alloc), buf, buf, 1, None, 0) == _lib.STATUS_NULL_ARGUMENT
     alloc = _lib.PageAllocator(16, 16, 16, 16, 16, 16, 16, 0, 16, 4, 8)
     assert h.sdc_pages_fork(ctypes.byref(alloc), buf, buf, 1, None, 0) == _lib.STATUS_INVALID_SIZE
+
+
+def test_head_gather_entry_points_validate_on_the_host(lib):
+    """The fused head gather refuses bad rank / world / epoch and null
+    destination arrays before any device work; the peer-buffer helpers
+    refuse null and short arguments."""
+    h = lib.handle
+    pool = _lib.PagePool(16, 16, 16, 16, 4, 2, 1, 1, 128, 2048, 2048, 2048, 16, 16, 16)
+    buf = ctypes.c_void_p(256)  # never dereferenced
+    outs = (ctypes.c_void_p * 2)(256, 512)
+    flags = (ctypes.c_void_p * 2)(1024, 2048)
+    status = ctypes.c_void_p(4096)
+
+    def call(outs_, flags_, world, rank, epoch):
+        return h.sdc_paged_verify_attention_gather(ctypes.byref(pool), 0, buf, _lib.DTYPE_BF16, 1, 4, 1, buf, 1,
+                                                   buf, 16, outs_, flags_, world, rank, epoch, buf, 1 << 20,
+                                                   status, 0)
+
+    assert call(None, flags, 2, 0, 1) == _lib.STATUS_NULL_ARGUMENT
+    assert call(outs, None, 2, 0, 1) == _lib.STATUS_NULL_ARGUMENT
+    assert call(outs, flags, 9, 0, 1) == _lib.STATUS_INVALID_ARGUMENT
+    assert call(outs, flags, 0, 0, 1) == _lib.STATUS_INVALID_ARGUMENT
+    assert call(outs, flags, 2, 2, 1) == _lib.STATUS_INVALID_ARGUMENT
+    assert call(outs, flags, 2, -1, 1) == _lib.STATUS_INVALID_ARGUMENT
+    assert call(outs, flags, 2, 0, 0) == _lib.STATUS_INVALID_ARGUMENT
+    misaligned = (ctypes.c_void_p * 2)(256, 520)
+    assert call(misaligned, flags, 2, 0, 1) == _lib.STATUS_MISALIGNED
+    ptr = ctypes.c_void_p()
+    assert h.sdc_peer_buffer_alloc(64, None) == _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_peer_buffer_alloc(0, ctypes.byref(ptr)) == _lib.STATUS_INVALID_SIZE
+    handle = (ctypes.c_char * _lib.PEER_HANDLE_BYTES)()
+    assert h.sdc_peer_buffer_export(None, handle, len(handle)) == _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_peer_buffer_export(buf, handle, 8) == _lib.STATUS_INVALID_SIZE
+    assert h.sdc_peer_buffer_open(handle, 8, ctypes.byref(ptr)) == _lib.STATUS_INVALID_SIZE
+    assert h.sdc_peer_buffer_open(None, len(handle), ctypes.byref(ptr)) == _lib.STATUS_NULL_ARGUMENT
+    assert h.sdc_peer_buffer_free(None) == _lib.STATUS_OK
+    assert h.sdc_peer_buffer_close(None) == _lib.STATUS_OK
