@@ -172,3 +172,53 @@ def test_head_gather_entry_points_validate_on_the_host(lib):
     assert h.sdc_peer_buffer_open(None, len(handle), ctypes.byref(ptr)) == _lib.STATUS_NULL_ARGUMENT
     assert h.sdc_peer_buffer_free(None) == _lib.STATUS_OK
     assert h.sdc_peer_buffer_close(None) == _lib.STATUS_OK
+
+
+COMPAT_HEADER = Path(__file__).resolve().parents[1] / "include" / "specdecode_native_compat.h"
+
+
+def test_reference_native_symbols_are_exported(lib):
+    """The nine sd_* names the reference's loader binds (native.py:93-153)
+    are declared in the compatibility header and exported, and no others."""
+    import subprocess
+
+    declared = sorted(set(re.findall(r"SDC_API\s+[\w\s\*]+?\b(sd_\w+)\s*\(", COMPAT_HEADER.read_text())))
+    assert len(declared) == 9
+    out = subprocess.run(["nm", "-D", "--defined-only", lib.path], capture_output=True, text=True, check=True)
+    exported = sorted({line.split()[-1] for line in out.stdout.splitlines() if " T sd_" in line})
+    assert exported == declared
+    h = ctypes.CDLL(lib.path)
+    h.sd_abi_version.restype = ctypes.c_uint32
+    assert h.sd_abi_version() == 0x00010001
+
+
+def test_reference_loader_accepts_the_library(lib):
+    """The reference's own ctypes loader (its _NativeLibrary, unchanged from
+    oracle/_ref) loads libspecdecode_cuda.so, checks its ABI version and
+    binds every function; its status strings equal the reference library's,
+    and the checks that need no device give the reference's statuses."""
+    from oracle.reference_runs import ReferenceUnavailable, reference_package
+
+    try:
+        reference_package()
+    except ReferenceUnavailable as error:
+        pytest.skip(str(error))
+    from specdecode import native as ref_native
+
+    ours = ref_native._NativeLibrary(lib.path)
+    theirs = ref_native._NativeLibrary(str(Path(ref_native.__file__).resolve().parents[1] /
+                                           "libspecdecode_native.so"))
+    for status in range(12):
+        assert ours.handle.sd_status_string(status) == theirs.handle.sd_status_string(status), status
+    d = (ctypes.c_double * 3)(0.2, 0.3, 0.5)
+    token = ctypes.c_uint64()
+    for h in (ours.handle, theirs.handle):
+        assert h.sd_sample_categorical_f64(d, 3, 0.5, None) == 1
+        assert h.sd_sample_categorical_f64(d, 3, 1.0, ctypes.byref(token)) == 7
+        assert h.sd_sample_categorical_f64(d, 0, 0.5, ctypes.byref(token)) == 2
+        assert h.sd_normalize_f64(d, 3, None) == 1
+        tok = (ctypes.c_uint64 * 1)(0)
+        assert h.sd_acceptance_probabilities_f64(d, d, tok, 0, 3, d) == 2
+        accepted, index = ctypes.c_size_t(9), ctypes.c_size_t(9)
+        assert h.sd_first_rejection_f64(None, None, 0, ctypes.byref(accepted), ctypes.byref(index)) == 0
+        assert (accepted.value, index.value) == (0, 0)
