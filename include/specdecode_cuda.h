@@ -226,7 +226,7 @@ SDC_API sdc_status_t sdc_paged_verify_attention(
  * output launches, one more launch stores `epoch` into flag `rank` of every
  * rank (release, system scope) and waits until this rank's flags all read
  * `epoch` (acquire): when it ends, this rank's buffer holds every rank's rows.
- * A wait that runs past about a second records SDC_FAULT_WAIT_TIMEOUT in
+ * A wait that runs past about nine seconds records SDC_FAULT_WAIT_TIMEOUT in
  * device_status and ends.  `epoch` must differ from the previous call's (a
  * per-call counter starting at 1; flag words start at 0).  Every rank must
  * make the same calls in the same order.  No counterpart in the reference,

@@ -128,6 +128,9 @@ struct SignalArgs {
 };
 
 __global__ void __launch_bounds__(32) gather_signal_kernel(SignalArgs s) {
+    // launched as a programmatic dependent of the output launch: this waits
+    // until that grid has finished and its stores are performed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int p = threadIdx.x;
     if (p >= s.world) return;
     __threadfence_system();
@@ -154,9 +157,22 @@ sdc_status_t launch_gather_signal(uint32_t* const* flags, int32_t world, int32_t
     s.world = world;
     s.rank = rank;
     s.epoch = epoch;
-    s.wait_limit = tc::wait_limit_cycles();
+    // ranks reach this point at different times (each rank's own host work
+    // comes first), so the default bound is eight times the pipeline
+    // waits' (about 9 s); a shorter test limit applies as set
+    const long long limit = tc::wait_limit_cycles();
+    s.wait_limit = limit >= (1ll << 31) ? (1ll << 34) : limit;
     s.status = status;
-    gather_signal_kernel<<<1, 32, 0, stream>>>(s);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, gather_signal_kernel, s) != cudaSuccess) return SDC_STATUS_CUDA_ERROR;
     return launch_status();
 }
 

@@ -298,6 +298,9 @@ template <typename QT>
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(AttnArgs a) {
     extern __shared__ float csm[];  // ml [chunks][group rows][2], then weights [chunks][group rows]
     asm volatile("griddepcontrol.wait;" ::: "memory");  // partials of the item kernel (no-op for a plain launch)
+    // a completion launch chained after this one (the KV-head gather's flags)
+    // may be scheduled now; it waits for this grid's stores before it signals
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int64_t item = blockIdx.x;
     const int64_t b = item / a.kv_heads;
     const int64_t h = item - b * a.kv_heads;
