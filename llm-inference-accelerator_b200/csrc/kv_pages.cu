@@ -321,7 +321,7 @@ struct RollbackArgs {
 // whole 128-byte rows at head_dim 128), then the span's 2 x heads scales per
 // layer.  The slot is read once per block and every store after it is
 // independent, so a block issues all of its writes back to back; the host
-// sizes the spans so that the grid covers every SM a few times over.
+// sizes the spans so that the grid fills every SM with eight blocks.
 __global__ void __launch_bounds__(256) rollback_kernel(RollbackArgs a) {
     if (blockIdx.x >= a.slot_blocks) {
         apply_table_edits(a.edits, threadIdx.x, blockDim.x, a.status);
@@ -752,9 +752,10 @@ SDC_API sdc_status_t sdc_rollback(const sdc_page_pool_t* pool, const int64_t* cl
         a.pool = to_pool(pool);
         a.slots = clear_slots;
         // layers per block: the whole slot when there are enough slots to
-        // cover every SM four times, otherwise spans small enough that they do
+        // fill every SM with eight blocks, otherwise spans small enough that
+        // they do (more resident warps hide the slot read before the stores)
         const int64_t L = pool->num_layers;
-        const int64_t want = 4 * static_cast<int64_t>(device_sms());
+        const int64_t want = 8 * static_cast<int64_t>(device_sms());
         const int64_t splits = num_clear > 0 ? std::min<int64_t>(L, ceil_div(want, num_clear)) : 1;
         const int64_t span = ceil_div(L, splits);
         const int64_t spans = ceil_div(L, span);

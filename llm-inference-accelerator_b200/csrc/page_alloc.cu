@@ -266,7 +266,8 @@ struct TruncateArgs {
     int32_t sequences;
     int64_t max_removed;
     int32_t* status;
-    int64_t span;  // layers one zeroing block clears
+    int64_t span;      // layers one zeroing block clears
+    FastDiv div_pairs;  // 2 x heads: a (layer, key/value head) pair index into its parts
 };
 
 __device__ __forceinline__ bool truncate_valid(const TruncateArgs& t, int s, int32_t* row, int64_t* old, int64_t* now) {
@@ -314,11 +315,13 @@ __global__ void __launch_bounds__(kPlanThreads) truncate_mark_kernel(TruncateArg
     }
 }
 
+// (layer, key/value head) pairs one zeroing block clears at most.
+constexpr int kZeroPairs = 512;
+
 // Block (touched page j, row s, layer span z) zeroes the rows to clear of
 // that page in the span's layers -- every head, keys and values, codes and
-// scales -- one 16-byte chunk per thread and step.  The page's checks are
-// made once per block; the host sizes the spans so that the grid still
-// covers every SM a few times over.
+// scales.  The page's checks are made once per block; the host sizes the
+// spans so that the grid still covers every SM several times over.
 __global__ void __launch_bounds__(kCopyThreads) truncate_zero_kernel(TruncateArgs t) {
     const Alloc& a = t.a;
     const Pool& pool = t.pool;
@@ -344,30 +347,46 @@ __global__ void __launch_bounds__(kCopyThreads) truncate_zero_kernel(TruncateArg
     }
     const int rows = a.high_water[blk] - first;
     if (rows <= 0) return;
+    // The span's (layer, key/value head) pairs each hold `rows` contiguous
+    // rows to clear (rows x head_dim bytes) and `rows` scales.  The block
+    // first lays out every pair's code and scale addresses in shared memory;
+    // then threads walk the flattened (pair, 16-byte chunk) space in
+    // block-strided order with incremental indices, so a store costs one
+    // shared load and an add.
+    __shared__ int8_t* code_at[kZeroPairs];
+    __shared__ float* scale_at[kZeroPairs];
     const int H = static_cast<int>(pool.num_heads);
-    const int row_chunks = static_cast<int>(pool.head_dim / 16);
-    const int per_head = rows * row_chunks;
-    const int per_layer = 2 * H * per_head;
-    int8_t* const keys = pool.keys + blk * pool.cbs + layer0 * pool.cls + first * pool.head_dim;
-    int8_t* const values = pool.values + blk * pool.cbs + layer0 * pool.cls + first * pool.head_dim;
-    for (int c = threadIdx.x; c < layers * per_layer; c += blockDim.x) {
-        const int layer = c / per_layer, in_layer = c - layer * per_layer;
-        const int kvh = in_layer / per_head, rem = in_layer - kvh * per_head;
-        const bool value_side = kvh >= H;
-        const int head = value_side ? kvh - H : kvh;
-        // a head's rows to clear are contiguous: rem indexes their 16-byte chunks
-        int8_t* codes = (value_side ? values : keys) + layer * pool.cls + head * pool.chs + rem * 16;
-        *reinterpret_cast<uint4*>(codes) = make_uint4(0u, 0u, 0u, 0u);
+    const int pairs = layers * 2 * H;  // <= kZeroPairs (the host sizes the span)
+    for (int pr = static_cast<int>(threadIdx.x); pr < pairs; pr += static_cast<int>(blockDim.x)) {
+        uint32_t layer, kvh;
+        t.div_pairs.divmod(static_cast<uint32_t>(pr), layer, kvh);
+        const bool value_side = static_cast<int>(kvh) >= H;
+        const int64_t head = value_side ? static_cast<int>(kvh) - H : static_cast<int>(kvh);
+        const int64_t l = layer0 + layer;
+        code_at[pr] = (value_side ? pool.values : pool.keys) + blk * pool.cbs + l * pool.cls + head * pool.chs +
+                      first * pool.head_dim;
+        scale_at[pr] = (value_side ? pool.value_scales : pool.key_scales) + blk * pool.sbs + l * pool.sls +
+                       head * pool.shs + first;
     }
-    const int scales_per_layer = 2 * H * rows;
-    for (int i = threadIdx.x; i < layers * scales_per_layer; i += blockDim.x) {
-        const int layer = i / scales_per_layer, in_layer = i - layer * scales_per_layer;
-        const int kvh = in_layer / rows, r = first + in_layer % rows;
-        const bool value_side = kvh >= H;
-        const int head = value_side ? kvh - H : kvh;
-        float* scales = value_side ? pool.value_scales : pool.key_scales;
-        scales[blk * pool.sbs + (layer0 + layer) * pool.sls + head * pool.shs + r] = 0.0f;
-    }
+    __syncthreads();
+    auto walk = [&](int per_pair, auto&& store) {
+        const int step = static_cast<int>(blockDim.x);
+        const int dq = step / per_pair, dr = step - dq * per_pair;
+        int pr = static_cast<int>(threadIdx.x) / per_pair;
+        int j = static_cast<int>(threadIdx.x) - pr * per_pair;
+        while (pr < pairs) {
+            store(pr, j);
+            j += dr;
+            pr += dq;
+            if (j >= per_pair) {
+                j -= per_pair;
+                ++pr;
+            }
+        }
+    };
+    walk(rows * static_cast<int>(pool.head_dim / 16),
+         [&](int pr, int c) { *reinterpret_cast<uint4*>(code_at[pr] + c * 16) = make_uint4(0u, 0u, 0u, 0u); });
+    walk(rows, [&](int pr, int r) { scale_at[pr][r] = 0.0f; });
 }
 
 __global__ void __launch_bounds__(kPlanThreads) truncate_finish_kernel(TruncateArgs t) {
@@ -517,23 +536,28 @@ SDC_API sdc_status_t sdc_pages_truncate(const sdc_page_allocator_t* allocator, c
         if (sequences < 1 || sequences > 65535 || max_removed < 0) return SDC_STATUS_INVALID_SIZE;
         if (max_removed > 65535) return SDC_STATUS_OVERFLOW;
         TruncateArgs t{a, to_pool(pool), rows, new_lengths, static_cast<int32_t>(sequences), max_removed,
-                       device_status, 1};
-        cudaStream_t s = as_stream(stream);
-        const unsigned row_blocks = static_cast<unsigned>(ceil_div(sequences, kPlanThreads));
-        truncate_mark_kernel<<<row_blocks, kPlanThreads, 0, s>>>(t);
+                       device_status, 1, FastDiv(static_cast<uint32_t>(2 * pool->num_heads))};
+        // zeroing grid, checked before anything launches: pages a truncation
+        // of at most max_removed tokens touches, and layers per block -- as
+        // many as keep the grid at four blocks per SM or more
+        const int64_t pages = (max_removed + a.block_size - 1) / a.block_size + 1;
+        int64_t spans = 1;
         if (max_removed > 0) {
-            // pages a truncation of at most max_removed tokens touches
-            const int64_t pages = (max_removed + a.block_size - 1) / a.block_size + 1;
-            // layers per block: as many as keep the grid at four blocks per SM or more
+            if (2 * pool->num_heads > kZeroPairs) return SDC_STATUS_UNSUPPORTED;
             const int64_t L = pool->num_layers;
             const int64_t splits = std::min<int64_t>(L, ceil_div(4 * static_cast<int64_t>(device_sms()),
                                                                  pages * sequences));
-            t.span = ceil_div(L, splits);
-            const int64_t spans = ceil_div(L, t.span);
+            t.span = std::min<int64_t>(ceil_div(L, splits), kZeroPairs / (2 * pool->num_heads));
+            spans = ceil_div(L, t.span);
             if (spans > 65535 || pages > INT32_MAX) return SDC_STATUS_UNSUPPORTED;
             if (t.span * 2 * pool->num_heads * a.block_size * (pool->head_dim / 16) >= INT32_MAX) {
                 return SDC_STATUS_OVERFLOW;
             }
+        }
+        cudaStream_t s = as_stream(stream);
+        const unsigned row_blocks = static_cast<unsigned>(ceil_div(sequences, kPlanThreads));
+        truncate_mark_kernel<<<row_blocks, kPlanThreads, 0, s>>>(t);
+        if (max_removed > 0) {
             truncate_zero_kernel<<<dim3(static_cast<unsigned>(pages), static_cast<unsigned>(sequences),
                                         static_cast<unsigned>(spans)),
                                    kCopyThreads, 0, s>>>(t);
