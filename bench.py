@@ -16,9 +16,14 @@ sequences appending a 5-token window per step, 0-5 tokens rolled back each,
 
 Inputs are synthetic (seeded N(0,1) K/V and queries, there is no dataset for
 this path).  L2 is flushed (a 256 MiB write) between timed iterations, and
-each pool is larger than L2.  ``--impl reference`` times the reference's CPU
-path (the oracle's restatement of its unfused dequantize-then-SDPA op, all
-host threads) on a bounded sample of the same workload.
+each pool is larger than L2.  ``--impl reference`` times the reference's own
+CPU path on this host (its unchanged Python package and C++ quantizer,
+copied and built into oracle/_ref by ``make -C oracle ref``): its
+submit_paged_attention on CPU torch with all host threads (the headline
+value), its materialize_legacy_cache reconstruct path with torch CPU SDPA,
+and its PagedKVCache append / truncate with NativeKVQuantizer, each on a
+bounded sample of the same workloads.  The same measurements are reported
+beside this library's numbers as ``cpu_baseline`` blocks.
 """
 
 from __future__ import annotations
@@ -93,6 +98,11 @@ def parse_args(argv=None):
                    help="skip the device acceptance/sampling workload (64 sequences x 6 proposals x 128256 tokens)")
     p.add_argument("--profile-sampling", action="store_true",
                    help="the acceptance/sampling workload only, a few rounds, no timing: for ncu")
+    p.add_argument("--profile-case", choices=("decode", "gather", "simt", "pages"),
+                   help="a few untimed calls of one kernel family for ncu: decode-shape attention (64 sequences "
+                        "x ~1100 tokens, head_dim 128 and 64, windows 1 and 6), the gather-dequantize of the "
+                        "verify batch, the CUDA-core attention kernel (head_dim 256), or the device allocator's "
+                        "append / truncate step")
     p.add_argument("--profile", action="store_true",
                    help="verify attention only: no clock sampling, sustained load, host-buffer pass, append "
                         "workload or CPU baseline (a short, repeatable run for ncu)")
@@ -108,8 +118,12 @@ def measured_peaks():
 
 
 def profiled_traffic(name: str):
-    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md
-    (a line ``traffic_bytes_per_launch: N``), or None."""
+    """Per-launch DRAM bytes of the dominant kernel, transcribed from the
+    committed ncu summary profiles/<name>.md (its line
+    ``traffic_bytes_per_launch: N``, dram__bytes_read.sum +
+    dram__bytes_write.sum of one captured launch), or None.  The figure is
+    read from that file, not measured by this run: ncu cannot run inside the
+    timed benchmark."""
     path = REPO / "profiles" / f"{name}.md"
     if not path.is_file():
         return None
@@ -464,11 +478,22 @@ def run_speculative(seed: int, device, world: int):
             session.timed = True
             session.timings.clear()
         eager_result, eager_prefill_ms, eager_decode_ms = timed_run()
-    attn = {}
+        attn = {}
+        for name, session in (("draft", dec.draft), ("target", dec.target)):
+            ms, nbytes = session.attention_time()
+            attn[name] = (ms, nbytes, len(session.timings))
+            # once more, each attention call's launches queued behind a
+            # device hold before its start event: device time per call
+            session.timings.clear()
+            session.timing_hold_cycles = HOLD_CYCLES
+        timed_run()
+    by_kind = {}
     for name, session in (("draft", dec.draft), ("target", dec.target)):
-        ms, nbytes = session.attention_time()
-        attn[name] = (ms, nbytes, len(session.timings))
+        for kind, (n, kms, kb) in session.attention_time_by_kind().items():
+            by_kind[f"{name}_{kind}"] = {"calls": n, "ms": kms, "us_per_call": 1e3 * kms / n,
+                                         "gbs": kb / (kms / 1e3) / 1e9 if kms > 0 else None}
         session.timed = False
+        session.timing_hold_cycles = 0
     peak, peak_kind = measured_peaks()
     tokens_out = B * sp["new_tokens"]
     decode_max = max_over_ranks(decode_ms, world)
@@ -495,6 +520,11 @@ def run_speculative(seed: int, device, world: int):
         "attention_gbs": attn_bytes / (attn_ms / 1e3) / 1e9 if attn_ms > 0 else None,
         "attention_fraction_of_peak": attn_bytes / (attn_ms / 1e3) / 1e9 / peak if attn_ms > 0 else None,
         "attention_calls": {k: v[2] for k, v in attn.items()},
+        # the eager run's attention calls by model and kind: prompt windows
+        # ("prefill"), single-token draft steps ("decode"), target windows of
+        # the proposals ("verify"); device time of each call (a rerun with a
+        # device hold queued before every call's start event)
+        "attention_by_kind": by_kind,
         "peak_source": peak_kind,
     }
     del dec, draft, target
@@ -628,7 +658,69 @@ def profile_append(seed: int, device, steps: int) -> None:
     print(json.dumps({"profile_append": True, "steps": steps}))
 
 
-def run_device_pages(seed: int, device, steps: int, warmup: int, world: int):
+def profile_case(name: str, seed: int, device, calls: int) -> None:
+    """``calls`` untimed calls of one kernel family, then a fault check: the
+    small, repeatable runs the ncu summaries are captured on."""
+    import numpy as np
+    import torch
+
+    from specdecode_b200.cuda_kv_cache import PagedVerifyAttention
+    from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
+
+    def filled_cache(lens, heads, dim, layers=1):
+        nblk = (np.asarray(lens) + 15) // 16
+        cache = PagedKVCache(KVCacheConfig(layers, heads, dim, block_size=16, num_blocks=int(nblk.sum())),
+                             device=device, max_sequences=len(lens), check_status=False,
+                             max_blocks_per_sequence=int(nblk.max()))
+        gen = torch.Generator(device=device).manual_seed(seed)
+        for b, T in enumerate(lens):
+            cache.create_sequence(b)
+            shape = (int(T), layers, heads, dim)
+            cache.append_tensor(b, torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16),
+                                torch.randn(shape, generator=gen, device=device, dtype=torch.bfloat16))
+        return cache
+
+    def attend(cache, lens, query_heads, windows):
+        attention = PagedVerifyAttention.for_cache(cache)
+        tables, ctx, max_len = cache.attention_inputs(list(range(len(lens))))
+        gen = torch.Generator(device=device).manual_seed(seed + 1)
+        queries = [torch.randn((len(lens), query_heads, window, cache.config.head_dim), generator=gen,
+                               device=device).to(torch.bfloat16) for window in windows]
+        for _ in range(calls):  # the windows interleaved: one launch of each per round
+            for q in queries:
+                attention(q, tables, ctx, max_len, 0)
+
+    rng = np.random.default_rng(seed + 5)
+    if name == "decode":
+        lens = rng.integers(1024, 1177, size=64).tolist()
+        for dim in (128, 64):
+            cache = filled_cache(lens, 8, dim)
+            attend(cache, lens, 32, (1, 6))
+            torch.cuda.synchronize()
+            if cache.status_bits():
+                raise RuntimeError("device fault in the decode-shape profile run")
+            del cache
+    elif name == "simt":
+        lens = rng.integers(1024, 4097, size=16).tolist()
+        cache = filled_cache(lens, 8, 256)
+        attend(cache, lens, 32, (5,))
+        torch.cuda.synchronize()
+        if cache.status_bits():
+            raise RuntimeError("device fault in the CUDA-core attention profile run")
+    elif name == "gather":
+        state = build_verify(seed, device)
+        slots = verify_slots(state, device)
+        for _ in range(calls):
+            state["cache"].gather_slots(slots, torch.bfloat16)
+        torch.cuda.synchronize()
+        if state["cache"].status_bits():
+            raise RuntimeError("device fault in the gather profile run")
+    elif name == "pages":
+        run_device_pages(seed, device, max(1, calls // 2), max(1, calls - calls // 2), 1, num_blocks=4096)
+    print(json.dumps({"profile_case": name, "calls": calls}))
+
+
+def run_device_pages(seed: int, device, steps: int, warmup: int, world: int, num_blocks: int | None = None):
     """The append workload's speculative step (256 sequences append 5 tokens
     to 32 layers x 8 heads, then roll back 0-5 of them) with the block tables,
     lengths and free set on the device (DevicePagedCache): planning is a
@@ -643,10 +735,11 @@ def run_device_pages(seed: int, device, steps: int, warmup: int, world: int):
 
     a = APPEND
     rng = np.random.default_rng(seed + 1)
+    nb = a["num_blocks"] if num_blocks is None else num_blocks
     cache = DevicePagedCache(KVCacheConfig(a["layers"], a["kv_heads"], a["head_dim"], block_size=a["block_size"],
-                                           num_blocks=a["num_blocks"]),
+                                           num_blocks=nb),
                              max_rows=a["sequences"], max_blocks_per_row=512,
-                             block_order=rng.permutation(a["num_blocks"]), device=device)
+                             block_order=rng.permutation(nb), device=device)
     rows = list(range(a["sequences"]))
     gen = torch.Generator(device=device).manual_seed(seed + 2)
     shape = (a["sequences"], a["window"], a["layers"], a["kv_heads"], a["head_dim"])
@@ -780,6 +873,118 @@ def run_sampling(seed: int, device, steps: int, warmup: int, profile_only: bool 
     }
 
 
+def verify_slots(state, device):
+    """Physical slots of every cached token of the verify batch, sequence by
+    sequence in context order (block table entry * block_size + offset): the
+    token list a dequantize-then-attend caller gathers for one layer."""
+    import numpy as np
+    import torch
+
+    bs = VERIFY["block_size"]
+    parts = []
+    for b, T in enumerate(state["lens"].tolist()):
+        pos = np.arange(T, dtype=np.int64)
+        parts.append(state["table"][b, pos // bs].astype(np.int64) * bs + pos % bs)
+    return torch.from_numpy(np.concatenate(parts)).to(device)
+
+
+def run_gather(state, device, steps: int, warmup: int, flush):
+    """``sdc_gather_dequantize`` over the verify batch: every cached token of
+    its 32 sequences (one layer, 8 KV heads x 128) dequantized to bf16, the
+    reconstruct that a dequantize-then-attend path performs before its
+    attention.  Device time per call, L2 flushed between calls; algorithmic
+    bytes: per token and KV head the 2 x 128 codes and 2 scales read and the
+    2 x 128 bf16 values written, plus the 8-byte slot."""
+    import torch
+
+    cache = state["cache"]
+    slots = verify_slots(state, device)
+    n = int(slots.numel())
+    H, D = VERIFY["kv_heads"], VERIFY["head_dim"]
+    out = (torch.empty((n, 1, H, D), dtype=torch.bfloat16, device=device),
+           torch.empty((n, 1, H, D), dtype=torch.bfloat16, device=device))
+    for _ in range(warmup):
+        flush.zero_()
+        cache.gather_slots(slots, torch.bfloat16, out=out)
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        hold_device()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        cache.gather_slots(slots, torch.bfloat16, out=out)
+        end.record()
+        times.append((start, end))
+    torch.cuda.synchronize()
+    if cache.status_bits():
+        raise RuntimeError("device fault in the gather workload")
+    ms = statistics.median(s.elapsed_time(e) for s, e in times)
+    nbytes = n * (H * (2 * D + 8 + 2 * D * 2) + 8)
+    peak, peak_kind = measured_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    del out
+    return {"workload": f"{n} cached tokens of the verify batch, one layer, 8 KV heads x 128, int8 pages -> bf16",
+            "us_per_call": 1e3 * ms, "algorithmic_bytes": nbytes, "gbs": gbs,
+            "frac_of_peak": gbs / peak if peak else None, "peak_source": peak_kind}
+
+
+def run_decode_shapes(seed: int, device, steps: int, warmup: int, flush):
+    """Stand-alone attention calls at the end-to-end workload's shapes: 64
+    sequences of about 1100 cached tokens, 32 query / 8 KV heads, a one-token
+    decode step and a six-token verify window, head_dim 128 (the target)
+    and 64 (the draft).  Device time per call with an L2 flush between
+    calls: the figures the end-to-end loop's attention calls compare to."""
+    import numpy as np
+    import torch
+
+    from specdecode_b200.cuda_kv_cache import PagedVerifyAttention, attention_bytes
+    from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
+
+    B, Hq, Hkv, bs = 64, 32, 8, 16
+    rng = np.random.default_rng(seed + 5)
+    lens = rng.integers(1024, 1177, size=B)
+    out = {}
+    for D in (128, 64):
+        nblk = (lens + bs - 1) // bs
+        nb = int(nblk.sum())
+        cache = PagedKVCache(KVCacheConfig(1, Hkv, D, block_size=bs, num_blocks=nb), device=device,
+                             max_sequences=B, check_status=False, max_blocks_per_sequence=int(nblk.max()))
+        gen = torch.Generator(device=device).manual_seed(seed + D)
+        for b in range(B):
+            cache.create_sequence(b)
+            T = int(lens[b])
+            cache.append_tensor(b, torch.randn((T, 1, Hkv, D), generator=gen, device=device, dtype=torch.bfloat16),
+                                torch.randn((T, 1, Hkv, D), generator=gen, device=device, dtype=torch.bfloat16))
+        attention = PagedVerifyAttention.for_cache(cache)
+        tables, ctx, max_len = cache.attention_inputs(list(range(B)))
+        for window in (1, 6):
+            q = torch.randn((B, Hq, window, D), generator=gen, device=device).to(torch.bfloat16)
+            res = torch.empty_like(q)
+            for _ in range(warmup):
+                flush.zero_()
+                attention(q, tables, ctx, max_len, 0, out=res)
+            times = []
+            for _ in range(steps):
+                flush.zero_()
+                hold_device()
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                attention(q, tables, ctx, max_len, 0, out=res)
+                end.record()
+                times.append((start, end))
+            torch.cuda.synchronize()
+            ms = statistics.median(s.elapsed_time(e) for s, e in times)
+            nbytes = attention_bytes(lens.tolist(), Hq, Hkv, D, window, bs)
+            out[f"d{D}_window{window}"] = {"us_per_call": 1e3 * ms, "gbs": nbytes / (ms / 1e3) / 1e9}
+        if cache.status_bits():
+            raise RuntimeError("device fault in the decode-shape workload")
+        del cache, attention
+        torch.cuda.empty_cache()
+    out["workload"] = ("64 sequences x 1024-1176 cached tokens, 32 query / 8 KV heads, block 16, one layer; "
+                       "median of the timed calls, L2 flushed between calls")
+    return out
+
+
 def run_long_context(seed: int, rank: int, world: int, device, steps: int, warmup: int):
     """Llama-3.1-70B long-context verify, one layer: 8 sequences x 131072
     tokens, 64 query / 8 KV heads, window 5.  KV heads are split over the
@@ -791,7 +996,7 @@ def run_long_context(seed: int, rank: int, world: int, device, steps: int, warmu
 
     from specdecode_b200.cuda_kv_cache import PagedVerifyAttention, attention_bytes
     from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
-    from specdecode_b200.sharding import TensorParallelVerifyAttention, head_shard, shard_query
+    from specdecode_b200.sharding import PeerHeadGather, TensorParallelVerifyAttention, head_shard, shard_query
 
     c = LONG
     shard = head_shard(rank, world, c["kv_heads"], c["query_heads"])
@@ -838,22 +1043,99 @@ def run_long_context(seed: int, rank: int, world: int, device, steps: int, warmu
 
     local_ms = timed(lambda: attention(q_local, tables, lens, T, 0, out=out_local))
     full_ms = timed(lambda: tp(query, tables, lens, T, 0))
+    peer_ms = None
+    if world > 1:
+        # the all-gather fused into the attention's output stores (peer
+        # stores over NVLink + bounded flag waits), against the NCCL one
+        gather = PeerHeadGather(cache, shard, B, kw)
+        try:
+            peer_ms = timed(lambda: gather(query, tables, lens, T, 0))
+            if not torch.equal(gather(query, tables, lens, T, 0), tp(query, tables, lens, T, 0)):
+                raise RuntimeError("the fused head gather and the NCCL all-gather disagree")
+        finally:
+            gather.close()
     if cache.status_bits():
         raise RuntimeError(f"device fault bits 0x{cache.status_bits():x} in the long-context benchmark")
     per_rank = attention_bytes([T] * B, shard.q_per_rank, shard.kv_per_rank, D, kw, bs)
     total = sum_over_ranks(per_rank, world)
+    shard_local = None
+    if world == 1:
+        del cache, attention, tp
+        torch.cuda.empty_cache()
+        shard_local = long_context_shards(seed, device, steps, warmup)
     return {
         "config": "70B long-context verify, one layer: B8 x 131072 tokens, Hq64 Hkv8 D128 window5 bs16, "
                   "randomly permuted blocks",
-        "parallelism": f"KV-head tensor-parallel x{world}" + (" + NCCL all-gather of outputs" if world > 1 else ""),
+        "parallelism": f"KV-head tensor-parallel x{world}" + (
+            "; outputs gathered by NCCL all-gather, or by the attention's own peer stores + flags (fused)"
+            if world > 1 else ""),
         "scaling": "strong",
         "gbs": total / (local_ms / 1e3) / 1e9,
         "ms_per_step": local_ms,
         "gbs_with_allgather": total / (full_ms / 1e3) / 1e9,
         "ms_per_step_with_allgather": full_ms,
+        "gbs_with_fused_gather": total / (peer_ms / 1e3) / 1e9 if peer_ms else None,
+        "ms_per_step_with_fused_gather": peer_ms,
         "allgather_bytes": B * c["query_heads"] * kw * D * 2 if world > 1 else 0,
         "algorithmic_bytes_per_step": total,
+        "shard_local": shard_local,
     }
+
+
+def long_context_shards(seed: int, device, steps: int, warmup: int):
+    """Rank 0's local attention in the long-context workload split over 2, 4
+    and 8 ranks, timed on this one GPU (its pages only: Hkv/G KV heads of
+    every sequence): how the per-GPU rate holds as the shard shrinks."""
+    import numpy as np
+    import torch
+
+    from specdecode_b200.cuda_kv_cache import PagedVerifyAttention, attention_bytes
+    from specdecode_b200.kv_cache import KVCacheConfig, PagedKVCache
+    from specdecode_b200.sharding import head_shard, shard_query
+
+    c = LONG
+    B, T, bs, D, kw = c["batch"], c["context"], c["block_size"], c["head_dim"], c["window"]
+    per_seq = T // bs
+    nb = B * per_seq
+    out = {}
+    for world in (2, 4, 8):
+        shard = head_shard(0, world, c["kv_heads"], c["query_heads"])
+        cache = PagedKVCache(KVCacheConfig(1, shard.kv_per_rank, D, block_size=bs, num_blocks=nb), device=device,
+                             max_sequences=1, check_status=False)
+        gen = torch.Generator(device=device).manual_seed(seed + world)
+        cache.create_sequence("fill")
+        for start in range(0, nb * bs, 1 << 16):
+            n = min(1 << 16, nb * bs - start)
+            k = torch.randn((n, 1, shard.kv_per_rank, D), generator=gen, device=device, dtype=torch.bfloat16)
+            v = torch.randn((n, 1, shard.kv_per_rank, D), generator=gen, device=device, dtype=torch.bfloat16)
+            cache.append_tensor("fill", k, v)
+        rng = np.random.default_rng(seed)
+        tables = torch.from_numpy(rng.permutation(nb).astype(np.int32).reshape(B, per_seq)).to(device)
+        lens = torch.full((B,), T, dtype=torch.int32, device=device)
+        query = torch.from_numpy(rng.standard_normal((B, c["query_heads"], kw, D), dtype=np.float32)).to(
+            torch.bfloat16).to(device)
+        q_local = shard_query(query, shard).contiguous()
+        attention = PagedVerifyAttention.for_cache(cache)
+        res = torch.empty_like(q_local)
+        for _ in range(warmup):
+            attention(q_local, tables, lens, T, 0, out=res)
+        times = []
+        for _ in range(steps):
+            hold_device()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            attention(q_local, tables, lens, T, 0, out=res)
+            end.record()
+            times.append((start, end))
+        torch.cuda.synchronize()
+        if cache.status_bits():
+            raise RuntimeError("device fault in the long-context shard timing")
+        ms = statistics.median(s.elapsed_time(e) for s, e in times)
+        nbytes = attention_bytes([T] * B, shard.q_per_rank, shard.kv_per_rank, D, kw, bs)
+        out[f"ranks{world}"] = {"kv_heads": shard.kv_per_rank, "ms": ms, "gbs": nbytes / (ms / 1e3) / 1e9}
+        del cache, attention
+        torch.cuda.empty_cache()
+    return out
 
 
 def verify_seq_bytes(lens):
@@ -1104,6 +1386,9 @@ def main(argv=None) -> int:
     if args.profile_sampling:
         run_sampling(args.seed, device, args.steps, args.warmup, profile_only=True)
         return 0
+    if args.profile_case:
+        profile_case(args.profile_case, args.seed, device, args.steps + args.warmup)
+        return 0
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
     state = build_verify(args.seed, device, rank, world)
 
@@ -1140,6 +1425,7 @@ def main(argv=None) -> int:
 
     e2e_ms, h2d, d2h = time_verify_e2e(state, args.steps, args.warmup, world, flush)
     e2e_value = total_bytes / (max_over_ranks(e2e_ms, world) / 1e3) / 1e9
+    gather = run_gather(state, device, args.steps, args.warmup, flush)
 
     append = None
     if not args.skip_append:
@@ -1148,6 +1434,10 @@ def main(argv=None) -> int:
     long_ctx = None
     if not args.skip_long:
         long_ctx = run_long_context(args.seed, rank, world, device, args.steps, args.warmup)
+
+    decode_shapes = None
+    if not args.skip_speculative:
+        decode_shapes = run_decode_shapes(args.seed + 1000 * rank, device, args.steps, args.warmup, flush)
 
     device_pages = None
     if not args.skip_device_pages:
@@ -1220,6 +1510,8 @@ def main(argv=None) -> int:
             "device_pages": device_pages,
             "speculative_sampling": sampling,
             "speculative_e2e": speculative,
+            "decode_shapes": decode_shapes,
+            "gather_dequantize": gather,
             "cpu_baseline": cpu,
             "clocks": clocks,
         }

@@ -78,6 +78,10 @@ class PagedAttentionSession:
         # optional device timing of the attention calls: (start, end, algorithmic bytes)
         self.timed = False
         self.timings: list = []
+        # with timing on: device cycles to hold the stream before each timed
+        # call's start event (torch.cuda._sleep), so that its launches are
+        # queued before the event runs and the interval is device time only
+        self.timing_hold_cycles = 0
         self._lengths: list[int] = []
         # fixed_step state: attention with its own workspace, so that device
         # addresses recorded in a CUDA graph stay valid
@@ -196,23 +200,26 @@ class PagedAttentionSession:
         group = Hq // Hkv
         window = max(1, _MAX_ROWS // group)
         if q_len <= window:
-            out = self._attend(query.contiguous(), tables, lens, max_len, layer, 0)
+            kind = "decode" if q_len == 1 else "verify"
+            out = self._attend(query.contiguous(), tables, lens, max_len, layer, 0, kind)
         else:
             parts = []
             for j in range(0, q_len, window):
                 w = min(window, q_len - j)
                 behind = q_len - (j + w)  # new tokens after this window
                 parts.append(self._attend(query[:, :, j:j + w].contiguous(), tables, lens - behind,
-                                          max_len - behind, layer, behind))
+                                          max_len - behind, layer, behind, "prefill"))
             out = torch.cat(parts, dim=2)
         return out.transpose(1, 2).contiguous(), None
 
-    def _attend(self, query, tables, lens, max_len, layer, behind):
+    def _attend(self, query, tables, lens, max_len, layer, behind, kind):
         if not self.timed or self._active_attention is not self.attention:
             return self._active_attention(query, tables, lens, max_len, layer)
         import torch
 
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if self.timing_hold_cycles > 0:
+            torch.cuda._sleep(int(self.timing_hold_cycles))
         start.record()
         out = self.attention(query, tables, lens, max_len, layer)
         end.record()
@@ -221,7 +228,7 @@ class PagedAttentionSession:
         per_token = 2 * cfg.num_heads * D + 2 * cfg.num_heads * 4
         nbytes = sum((t - behind) * per_token + -(-(t - behind) // cfg.block_size) * 4 for t in self._lengths)
         nbytes += 2 * B * Hq * w * D * query.element_size()
-        self.timings.append((start, end, nbytes))
+        self.timings.append((start, end, nbytes, kind))
         return out
 
     def attention_time(self) -> tuple[float, int]:
@@ -230,4 +237,17 @@ class PagedAttentionSession:
         import torch
 
         torch.cuda.synchronize()
-        return sum(s.elapsed_time(e) for s, e, _ in self.timings), sum(b for _, _, b in self.timings)
+        return sum(t[0].elapsed_time(t[1]) for t in self.timings), sum(t[2] for t in self.timings)
+
+    def attention_time_by_kind(self) -> dict[str, tuple[int, float, int]]:
+        """Per kind of call ("prefill" windows of a prompt, single-token
+        "decode" steps, multi-token "verify" windows): the timed calls' count,
+        milliseconds and algorithmic bytes (synchronises the device)."""
+        import torch
+
+        torch.cuda.synchronize()
+        out: dict[str, tuple[int, float, int]] = {}
+        for start, end, nbytes, kind in self.timings:
+            n, ms, b = out.get(kind, (0, 0.0, 0))
+            out[kind] = (n + 1, ms + start.elapsed_time(end), b + nbytes)
+        return out
