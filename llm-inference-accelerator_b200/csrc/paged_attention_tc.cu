@@ -62,6 +62,9 @@ constexpr float kRoundMagic = 12582912.0f;                  // 1.5 * 2^23
 constexpr int kMaxSplits = 2;
 // Largest work item in tiles (the chunk size is clamped to 16384 tokens).
 constexpr int kMaxItemTiles = 16384 / kTile;
+// What starting a work item costs an SM, in tiles (chunk sizing for long
+// contexts over few heads; measured on the 70B shards of one to eight GPUs).
+constexpr int64_t kItemStartTiles = 4;
 // Shared memory one block may use.
 constexpr int kSmemLimit = 232448;
 
@@ -1478,17 +1481,40 @@ bool supports(const AttnArgs& a) {
 }
 
 int64_t chunk_for(int64_t batch, int64_t kv_heads, int64_t max_context_len, int64_t rows) {
-    // about four items per SM when every sequence is at the maximum length;
-    // a multiple of the tile
-    const int64_t slots = static_cast<int64_t>(num_sms()) * 4;
+    const int64_t sms = static_cast<int64_t>(num_sms());
+    const int64_t pairs = batch * kv_heads * splits_for(rows);
+    // Fewer (sequence, KV head, row split) pairs than SMs: long contexts over
+    // few heads (a KV-head shard).  Every pair is taken to be at the maximum
+    // length, and the number of chunks per pair is the one whose busiest SM
+    // finishes first: ceil(pairs x n / SMs) items of ceil(tiles / n) tiles,
+    // each item's start counted as kItemStartTiles tiles.  (Four items per
+    // SM, the rule below, leaves some SMs a fifth item whenever the item
+    // count is not a multiple of the SM count.)
+    if (pairs < sms) {
+        const int64_t tiles = (max_context_len + kTile - 1) / kTile;
+        int64_t best_n = 0, best_cost = 0;
+        for (int64_t n = 1; n <= 256; ++n) {
+            const int64_t per = (tiles + n - 1) / n;
+            if (per > kMaxItemTiles) continue;
+            if (per * kTile < 512 && n > 1) break;
+            const int64_t cost = ((pairs * n + sms - 1) / sms) * (per + kItemStartTiles);
+            if (best_n == 0 || cost < best_cost) {
+                best_n = n;
+                best_cost = cost;
+            }
+        }
+        if (best_n > 0) return ((tiles + best_n - 1) / best_n) * kTile;
+    }
+    // otherwise about four items per SM when every sequence is at the
+    // maximum length; a multiple of the tile
+    const int64_t slots = sms * 4;
     int64_t c = (batch * kv_heads * splits_for(rows) * max_context_len + slots - 1) / slots;
     c = (c + kTile - 1) / kTile * kTile;
     if (c < 512) c = 512;
     if (c > kMaxItemTiles * kTile) c = kMaxItemTiles * kTile;
     // with at least two (sequence, KV head) items per SM, whole contexts
     // balance well enough and need no combine
-    if (batch * kv_heads * splits_for(rows) >= 2 * static_cast<int64_t>(num_sms()) &&
-        max_context_len <= kMaxItemTiles * kTile) {
+    if (pairs >= 2 * sms && max_context_len <= kMaxItemTiles * kTile) {
         c = (max_context_len + kTile - 1) / kTile * kTile;
     }
     return c;
