@@ -418,40 +418,64 @@ __device__ __forceinline__ void store16(__half* p, const int (&q)[16], float s) 
     d[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
+// Vectors each lane of the gather handles, a grid's width apart.
+constexpr int kGatherVectors = 2;
+
+// Each lane dequantizes 16 elements of a head vector (LPV lanes per vector)
+// for kGatherVectors vectors a grid's width apart: every vector's slot read,
+// then every code / scale read, is issued before any store, so that many
+// dependent load chains are in flight per lane.
 template <typename Out, int LPV>
 __global__ void __launch_bounds__(256) gather_dequantize_kernel(GatherArgs a) {
     constexpr int VPW = 32 / LPV;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t sub = lane & (LPV - 1);
     const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const uint32_t v = warp * VPW + lane / LPV;
-    if (v >= a.total_vectors) return;
+    const uint32_t pass = gridDim.x * (blockDim.x >> 5) * VPW;  // vectors one pass of the grid covers
     const uint32_t D = static_cast<uint32_t>(a.pool.head_dim);
-    uint32_t r, head, token, layer_rel;
-    a.div_heads.divmod(v, r, head);
-    const uint32_t kv = r & 1;
-    a.div_layers.divmod(r >> 1, token, layer_rel);
-    const int64_t slot = __ldg(a.slots + token);
-    if (slot < 0 || slot >= a.pool.num_blocks * a.pool.block_size) {
-        if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
-        return;
-    }
-    if (sub * 16 >= D) return;
-    uint32_t blk, off;
-    a.div_block.divmod(static_cast<uint32_t>(slot), blk, off);
-    const int64_t layer = a.layer_begin + layer_rel;
-    const int8_t* codes = (kv ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
-                          head * a.pool.chs + off * D + sub * 16;
-    const float s = __ldg((kv ? a.pool.value_scales : a.pool.key_scales) + blk * a.pool.sbs +
-                          layer * a.pool.sls + head * a.pool.shs + off);
-    const uint4 packed = __ldg(reinterpret_cast<const uint4*>(codes));
-    const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
-    int q[16];
+    constexpr int K = kGatherVectors;
+    uint32_t head[K], kv[K], token[K], layer_rel[K];
+    int64_t slot[K];
+    bool live[K];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) q[i] = static_cast<int8_t>((w[i / 4] >> (8 * (i % 4))) & 0xffu);
-    Out* dst = static_cast<Out*>(kv ? a.out_values : a.out_keys) + token * a.o_tok + layer_rel * a.o_layer +
-               head * a.o_head + sub * 16;
-    store16(dst, q, s);
+    for (int j = 0; j < K; ++j) {
+        const uint32_t v = warp * VPW + lane / LPV + j * pass;
+        live[j] = v < a.total_vectors && sub * 16 < D;
+        uint32_t r;
+        a.div_heads.divmod(live[j] ? v : 0u, r, head[j]);
+        kv[j] = r & 1;
+        a.div_layers.divmod(r >> 1, token[j], layer_rel[j]);
+        slot[j] = live[j] ? __ldg(a.slots + token[j]) : 0;
+    }
+    uint4 packed[K];
+    float scale[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        if (live[j] && (slot[j] < 0 || slot[j] >= a.pool.num_blocks * a.pool.block_size)) {
+            if (sub == 0) report_fault(a.status, SDC_FAULT_SLOT_RANGE);
+            live[j] = false;
+        }
+        if (!live[j]) continue;
+        uint32_t blk, off;
+        a.div_block.divmod(static_cast<uint32_t>(slot[j]), blk, off);
+        const int64_t layer = a.layer_begin + layer_rel[j];
+        const int8_t* codes = (kv[j] ? a.pool.values : a.pool.keys) + blk * a.pool.cbs + layer * a.pool.cls +
+                              head[j] * a.pool.chs + off * D + sub * 16;
+        scale[j] = __ldg((kv[j] ? a.pool.value_scales : a.pool.key_scales) + blk * a.pool.sbs +
+                         layer * a.pool.sls + head[j] * a.pool.shs + off);
+        packed[j] = __ldg(reinterpret_cast<const uint4*>(codes));
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        if (!live[j]) continue;
+        const uint32_t w[4] = {packed[j].x, packed[j].y, packed[j].z, packed[j].w};
+        int q[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q[i] = static_cast<int8_t>((w[i / 4] >> (8 * (i % 4))) & 0xffu);
+        Out* dst = static_cast<Out*>(kv[j] ? a.out_values : a.out_keys) + token[j] * a.o_tok +
+                   layer_rel[j] * a.o_layer + head[j] * a.o_head + sub * 16;
+        store16(dst, q, scale[j]);
+    }
 }
 
 constexpr int kThreads = 256;
@@ -820,7 +844,8 @@ SDC_API sdc_status_t sdc_gather_dequantize(const sdc_page_pool_t* pool, int64_t 
         a.o_layer = out_layer_stride;
         a.o_head = out_head_stride;
         a.status = device_status;
-        const int64_t blocks = vector_blocks(vectors, lpv);
+        // kGatherVectors vectors per lane, a grid's width apart
+        const int64_t blocks = vector_blocks((vectors + kGatherVectors - 1) / kGatherVectors, lpv);
         cudaStream_t st = as_stream(stream);
         switch (out_dtype) {
             case SDC_DTYPE_F32: return launch_gather<float>(lpv, blocks, st, a);
