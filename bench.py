@@ -925,7 +925,37 @@ def run_gather(state, device, steps: int, warmup: int, flush):
     del out
     return {"workload": f"{n} cached tokens of the verify batch, one layer, 8 KV heads x 128, int8 pages -> bf16",
             "us_per_call": 1e3 * ms, "algorithmic_bytes": nbytes, "gbs": gbs,
-            "frac_of_peak": gbs / peak if peak else None, "peak_source": peak_kind}
+            "frac_of_peak": gbs / peak if peak else None, "peak_source": peak_kind,
+            "storage_synchronize": time_storage_sync(state)}
+
+
+def time_storage_sync(state):
+    """``CudaPagedKVCacheStorage.synchronize`` over the verify pool's one
+    sequence (every cached page of the batch), wall clock: the first call
+    binds all tokens, later ones find nothing changed.  The pages already
+    live on the device, so a call is slot bookkeeping on the host; the
+    reference's storage uploads its CPU-side cache instead."""
+    from specdecode_b200.cuda_kv_cache import CudaPagedKVCacheStorage
+
+    cache = state["cache"]
+
+    class InlineRuntime:  # the runtime contract: run the transfer at once
+        device = cache.device
+
+        def submit_transfer(self, fn, *, wait_for=(), label=None):
+            return fn()
+
+    storage = CudaPagedKVCacheStorage(cache.config, InlineRuntime())
+    tokens = cache.sequence_length("fill")
+    t0 = time.perf_counter()
+    storage.synchronize(cache, "fill")
+    first = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    for _ in range(5):
+        storage.synchronize(cache, "fill")
+    again = (time.perf_counter() - t0) / 5
+    return {"tokens": tokens, "first_ms": 1e3 * first, "repeat_ms": 1e3 * again,
+            "tokens_per_s": tokens / first}
 
 
 def run_decode_shapes(seed: int, device, steps: int, warmup: int, flush):
