@@ -216,6 +216,12 @@ class CudaPagedKVCacheStorage:
         if self._sequence_id is not None and sequence_id != self._sequence_id:
             raise CudaPagedKVCacheError("CUDA paged-cache storage is already bound to another sequence")
         stable = cache.changes_since(sequence_id, self._tokens)
+        if cache is self._cache and sequence_id == self._sequence_id and stable == length == self._tokens:
+            # nothing appended or rolled back since the last call: the slots
+            # and block count are unchanged, nothing is uploaded or cleared
+            self._synchronizations += 1
+            view = self._view_of(cache, sequence_id, length)
+            return self.runtime.submit_transfer(lambda: view, label=f"specdecode.transfer.{self.name}.synchronize")
         table = cache.block_table(sequence_id)
         bs = self.config.block_size
         new_slots = tuple(table[t // bs] * bs + t % bs for t in range(length))
