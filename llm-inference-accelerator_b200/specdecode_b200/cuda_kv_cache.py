@@ -107,6 +107,7 @@ class PagedVerifyAttention:
         self.status = status
         self._workspace = None
         self._sizes: dict[tuple[int, int, int, int], int] = {}
+        self._checked_device = None  # self.device with its index, set on the first call
 
     @classmethod
     def for_cache(cls, cache: PagedKVCache) -> "PagedVerifyAttention":
@@ -140,6 +141,17 @@ class PagedVerifyAttention:
         query = query.contiguous()
         if out is None:
             out = torch.empty_like(query)
+        elif out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous():
+            raise CudaPagedAttentionError("out must be a contiguous tensor of the query's shape and dtype")
+        device = self._checked_device
+        if device is None:
+            device = torch.device(self.device)
+            if device.type == "cuda" and device.index is None:
+                device = torch.device("cuda", torch.cuda.current_device())
+            self._checked_device = device
+        if query.device != device or out.device != device or block_tables.device != device or \
+                context_lens.device != device:
+            raise CudaPagedAttentionError("query, out, block tables and context lengths must be on the pool's device")
         need = self.workspace_bytes(B, Hq, kw, int(max_context_len))
         if self._workspace is None or self._workspace.numel() < need:
             self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)

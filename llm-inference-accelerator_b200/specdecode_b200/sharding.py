@@ -243,6 +243,9 @@ class PeerHeadGather:
         B, hq, kw, _ = (int(d) for d in q.shape)
         if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
             raise ValueError("block tables and context lengths must be int32")
+        device = torch.device(self.cache.device)
+        if query.device != device or block_tables.device != device or context_lens.device != device:
+            raise ValueError("query, block tables and context lengths must be on the pool's device")
         block_tables = block_tables.contiguous()
         lib = self.library.handle
         need = self._attention_sizes.get(int(max_context_len))

@@ -288,3 +288,33 @@ def test_pipeline_wait_gives_up_and_reports(device, hq, window, d):
     assert cache.status_bits() == 0
     exact = attention_fp64(q[0].float().cpu().numpy(), *gather_oracle(keys, values, ks, vs, table, T, bs, 0))
     assert_near_exact(again[0].float().cpu().numpy(), exact, "after a timed-out launch", scale=3.0)
+
+
+def test_bad_output_or_device_is_refused_before_launch(device):
+    """An output buffer of another shape or dtype, or inputs left on the
+    host, raise before anything is launched (the kernel would otherwise write
+    past the buffer or read host addresses)."""
+    import torch
+
+    from specdecode_b200.cuda_kv_cache import CudaPagedAttentionError
+
+    rng = np.random.default_rng(3)
+    keys, values, ks, vs = random_pool(rng, 8, 16, 1, 8, 128)
+    cache = make_cache(device, 1, 8, 128, 16, 8)
+    load_logical(cache, keys, values, ks, vs)
+    q = torch.randn((1, 32, 5, 128), device=device).to(torch.bfloat16)
+    tables = tables_tensor([[0, 1, 2]], device)
+    lens = torch.tensor([40], dtype=torch.int32, device=device)
+    attention = _attention(cache)
+    for bad in (torch.empty((1, 32, 4, 128), dtype=torch.bfloat16, device=device),
+                torch.empty((1, 32, 5, 128), dtype=torch.float32, device=device),
+                torch.empty((1, 32, 5, 128), dtype=torch.bfloat16)):
+        with pytest.raises(CudaPagedAttentionError):
+            attention(q, tables, lens, 40, 0, out=bad)
+    with pytest.raises(CudaPagedAttentionError):
+        attention(q, tables.cpu(), lens, 40, 0)
+    torch.cuda.synchronize()
+    assert cache.status_bits() == 0
+    out = attention(q, tables, lens, 40, 0)
+    torch.cuda.synchronize()
+    assert cache.status_bits() == 0 and out.shape == q.shape
