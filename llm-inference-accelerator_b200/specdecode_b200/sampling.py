@@ -63,11 +63,32 @@ def _dtype(t) -> int:
 
 
 def _rows(t, name: str):
-    """A 2-D row batch with unit element stride (rows may be strided)."""
+    """A 2-D row batch on a CUDA device with unit element stride (rows may be
+    strided)."""
     if t.dim() != 2:
         raise ValueError(f"{name} must be [rows, vocab]")
+    _on_cuda(t, name)
     if t.stride(1) != 1:
         t = t.contiguous()
+    return t
+
+
+def _on_cuda(t, name: str) -> None:
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be on a CUDA device")
+
+
+def _aux(t, device, dtype):
+    """A small per-row input (uniforms, tokens, counts) as a contiguous
+    tensor of ``dtype`` on the rows' device (copied there if it is not)."""
+    return t.to(device=device, dtype=dtype).contiguous()
+
+
+def _out(t, shape, dtype, device, name: str):
+    """A caller-provided output: exactly the shape, dtype and device the
+    launch writes, contiguous."""
+    if tuple(t.shape) != tuple(shape) or t.dtype != dtype or t.device != device or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous {dtype} tensor of shape {tuple(shape)} on {device}")
     return t
 
 
@@ -82,6 +103,8 @@ def _status(status, device):
 
     if status is None:
         return torch.zeros(1, dtype=torch.int32, device=device)
+    if status.dtype != torch.int32 or status.device != device or status.numel() < 1:
+        raise ValueError(f"the status word must be an int32 tensor on {device}")
     return status
 
 
@@ -117,11 +140,13 @@ def sample_rows(weights, uniforms, *, out=None, status=None, library=None):
 
     lib = _library(library)
     w = _rows(weights, "weights")
-    u = uniforms.to(dtype=torch.float64).contiguous()
+    u = _aux(uniforms, w.device, torch.float64)
     if u.numel() != w.shape[0]:
         raise ValueError("one uniform per row is required")
     if out is None:
         out = torch.empty(w.shape[0], dtype=torch.int64, device=w.device)
+    else:
+        out = _out(out, (w.shape[0],), torch.int64, w.device, "out")
     st = _status(status, w.device)
     lib.check(lib.handle.sdc_sample_categorical_rows(w.data_ptr(), _dtype(w), w.shape[0], w.shape[1],
                                                      _stride(w, 0, w.shape[1]), u.data_ptr(), out.data_ptr(),
@@ -133,8 +158,8 @@ def sample_rows(weights, uniforms, *, out=None, status=None, library=None):
 def _pair(target, draft):
     t = _rows(target, "target")
     d = _rows(draft, "draft")
-    if t.shape != d.shape:
-        raise ValueError("target and draft rows must have the same shape")
+    if t.shape != d.shape or t.device != d.device:
+        raise ValueError("target and draft rows must have the same shape and device")
     if t.dtype != d.dtype:
         raise TypeError("target and draft rows must have the same dtype")
     return t, d
@@ -164,7 +189,7 @@ def acceptance_rows(target, draft, tokens, *, status=None, library=None):
 
     lib = _library(library)
     t, d = _pair(target, draft)
-    tok = tokens.to(dtype=torch.int64).contiguous()
+    tok = _aux(tokens, t.device, torch.int64)
     if tok.numel() != t.shape[0]:
         raise ValueError("one proposed token per row is required")
     out = torch.empty(t.shape[0], dtype=torch.float64, device=t.device)
@@ -183,8 +208,9 @@ def first_rejection_rows(probabilities, uniforms, *, status=None, library=None):
     import torch
 
     lib = _library(library)
+    _on_cuda(probabilities, "probabilities")
     p = probabilities.to(dtype=torch.float64).contiguous()
-    u = uniforms.to(dtype=torch.float64).contiguous()
+    u = _aux(uniforms, p.device, torch.float64)
     if p.dim() != 2 or p.shape != u.shape:
         raise ValueError("probabilities and uniforms must both be [sequences, proposals]")
     out = torch.empty(p.shape[0], dtype=torch.int64, device=p.device)
@@ -225,31 +251,41 @@ def verify_batch(target, draft, tokens, uniforms, *, proposal_counts=None, bonus
         raise ValueError("target must be [S, k + 1, V] and draft [S, k, V] with k >= 1")
     if target.dtype != draft.dtype:
         raise TypeError("target and draft rows must have the same dtype")
+    _on_cuda(target, "target")
+    if draft.device != target.device:
+        raise ValueError("target and draft rows must be on the same device")
+    dev = target.device
     if target.stride(2) != 1:
         target = target.contiguous()
     if draft.stride(2) != 1:
         draft = draft.contiguous()
-    tok = tokens.to(dtype=torch.int64)
+    tok = tokens.to(device=dev, dtype=torch.int64)
     if tok.dim() != 2 or tuple(tok.shape) != (S, k):
         raise ValueError("tokens must be [S, k]")
     if tok.stride(1) != 1:
         tok = tok.contiguous()
     u = uniforms
-    if u.dtype != torch.float64 or u.dim() != 2 or u.shape[0] != S or u.shape[1] < k + 1 or u.stride(1) != 1:
-        u = uniforms.to(dtype=torch.float64).contiguous()
+    if u.dtype != torch.float64 or u.device != dev or u.dim() != 2 or u.shape[0] != S or u.shape[1] < k + 1 or \
+            u.stride(1) != 1:
+        u = uniforms.to(device=dev, dtype=torch.float64).contiguous()
         if u.dim() != 2 or u.shape[0] != S or u.shape[1] < k + 1:
             raise ValueError("uniforms must be [S, >= k + 1]")
     counts = None
     if proposal_counts is not None:
-        counts = proposal_counts.to(dtype=torch.int64).contiguous()
+        counts = _aux(proposal_counts, dev, torch.int64)
+        if counts.numel() != S:
+            raise ValueError("proposal_counts must hold one count per sequence")
     bonus = None
     if bonus_allowed is not None:
-        bonus = bonus_allowed.to(dtype=torch.uint8).contiguous()
-    dev = target.device
-    accepted = out_accepted if out_accepted is not None else torch.empty(S, dtype=torch.int64, device=dev)
-    final = out_tokens if out_tokens is not None else torch.empty(S, dtype=torch.int64, device=dev)
-    probs = out_probabilities if out_probabilities is not None else torch.empty((S, k), dtype=torch.float64,
-                                                                                  device=dev)
+        bonus = _aux(bonus_allowed, dev, torch.uint8)
+        if bonus.numel() != S:
+            raise ValueError("bonus_allowed must hold one flag per sequence")
+    accepted = torch.empty(S, dtype=torch.int64, device=dev) if out_accepted is None else \
+        _out(out_accepted, (S,), torch.int64, dev, "out_accepted")
+    final = torch.empty(S, dtype=torch.int64, device=dev) if out_tokens is None else \
+        _out(out_tokens, (S,), torch.int64, dev, "out_tokens")
+    probs = torch.empty((S, k), dtype=torch.float64, device=dev) if out_probabilities is None else \
+        _out(out_probabilities, (S, k), torch.float64, dev, "out_probabilities")
     st = _status(status, dev)
     sums = torch.empty((S, k, 4), dtype=torch.float64, device=dev) if reuse_row_sums else None
     t_row = target.stride(1)

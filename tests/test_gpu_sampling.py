@@ -355,3 +355,30 @@ def test_large_vocabulary_round_properties(device):
         before = float(cum[c - 1]) if c > 0 else 0.0
         assert before <= thr + tol and thr < float(cum[c]) + tol, (s, c, before, thr)
     assert rejected > 0 and accepted > 0
+
+
+def test_host_inputs_and_wrong_outputs_are_refused_or_moved(device):
+    """Rows on the host, an output buffer or status word of the wrong kind
+    raise before a launch; small per-row inputs on the host are copied to the
+    rows' device."""
+    import torch
+
+    from specdecode_b200.sampling import sample_rows, verify_batch
+
+    w = torch.tensor([[0.2, 0.3, 0.5], [1.0, 0.0, 0.0]], dtype=torch.float64)
+    with pytest.raises(ValueError):
+        sample_rows(w, torch.tensor([0.5, 0.5], dtype=torch.float64))
+    wd = w.to(device)
+    got = sample_rows(wd, torch.tensor([0.6, 0.9], dtype=torch.float64))  # uniforms on the host
+    assert got.cpu().tolist() == [2, 0]
+    with pytest.raises(ValueError):
+        sample_rows(wd, torch.tensor([0.6, 0.9]), out=torch.empty(3, dtype=torch.int64, device=device))
+    with pytest.raises(ValueError):
+        sample_rows(wd, torch.tensor([0.6, 0.9]), status=torch.zeros(1, dtype=torch.int32))
+    target = torch.full((1, 2, 4), 0.25, dtype=torch.float64, device=device)
+    draft = torch.full((1, 1, 4), 0.25, dtype=torch.float64, device=device)
+    acc, tok, _ = verify_batch(target, draft, torch.tensor([[1]]), torch.tensor([[0.5, 0.1]], dtype=torch.float64))
+    assert acc.cpu().tolist() == [1] and 0 <= int(tok.item()) < 4
+    with pytest.raises(ValueError):
+        verify_batch(target, draft, torch.tensor([[1]]), torch.tensor([[0.5, 0.1]], dtype=torch.float64),
+                     out_accepted=torch.empty(2, dtype=torch.int64, device=device))
