@@ -76,6 +76,8 @@ class NativeKVQuantizer:
 
         if rows.dim() != 2:
             raise ValueError("rows must be a 2-D tensor")
+        if rows.device.type != "cuda":
+            raise ValueError("rows must be on a CUDA device")
         rows = rows.contiguous()
         n, count = rows.shape
         codes = torch.empty((n, count), dtype=torch.int8, device=rows.device)
